@@ -1,0 +1,405 @@
+"""Benchmark of the MXFP4 absorbed-MLA decode path on B200.
+
+Workload (per GPU, weak scaling across GPUs): Kimi-K2 decode shape -- 64
+heads, batch 64, every sequence 8192 tokens of paged MXFP4 latent (512) +
+bf16 RoPE (64), page size 64, seeded random-permutation page table,
+heads-first output, num_kv_splits automatic, sm_scale 1/sqrt(192).  Inputs
+are synthetic (seeded normal q and latents; the cache is written by this
+library's KV-append quantiser).  A step is one decode call over the whole
+batch (one layer).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  ``value`` is the aggregate achieved HBM
+bandwidth over all ranks computed from the algorithmic bytes (latent nibbles
++ e8m0 scales + RoPE of every token, plus q), divided by the max-over-ranks
+device time of the K timed steps; ``ms_per_step`` is the per-layer time.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "MLA decode µs/layer & achieved HBM TB/s (Kimi-K2, b64 ctx8K) at 1/2/4/8 B200"
+HEADS, BATCH, CTX, PAGE = 64, 64, 8192, 64
+SM_SCALE = 1.0 / math.sqrt(192.0)
+TOKEN_BYTES_ALGO = 256 + 16 + 128  # nibbles + e8m0 scales + bf16 RoPE per token
+FALLBACK_HBM_GBS = 6650.0
+WORKLOAD = (f"Kimi-K2 MXFP4 MLA decode: {HEADS} heads, batch {BATCH} per GPU, ctx {CTX} every sequence, "
+            f"page {PAGE}, seeded random-permutation page table, heads-first o, num_kv_splits auto")
+
+
+def algorithmic_bytes(batch=BATCH, heads=HEADS, ctx=CTX) -> int:
+    return batch * ctx * TOKEN_BYTES_ALGO + batch * heads * 576 * 2
+
+
+def _peak_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def _traffic_summary():
+    """ncu DRAM bytes per launch of the dominant kernel, from the committed
+    profile summary (profiles/decode_traffic.json), or None."""
+    path = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period: float = 0.02):
+        self.idx, self.period = device_index, period
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+            return self
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+                mask = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def build_workload(torch, kimi, dev, seed: int):
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    pages = BATCH * CTX // PAGE
+    kvb, kvs = kimi.alloc_mxfp4_cache(pages, dev, zero=False)
+    chunk = 1 << 16
+    for start in range(0, pages * PAGE, chunk):
+        n = min(chunk, pages * PAGE - start)
+        kv_c = torch.randn(n, 512, generator=gen, device=dev).to(torch.bfloat16)
+        k_pe = torch.randn(n, 64, generator=gen, device=dev).to(torch.bfloat16)
+        kimi.mxfp4_kv_append(kv_c, k_pe, kvb, kvs, torch.arange(start, start + n, device=dev))
+    perm = torch.randperm(pages, generator=gen, device=dev).to(torch.int32)
+    indptr = (torch.arange(BATCH + 1, device=dev, dtype=torch.int32) * (CTX // PAGE)).contiguous()
+    last = torch.full((BATCH,), PAGE, dtype=torch.int32, device=dev)
+    q = torch.randn(BATCH, HEADS, 576, generator=gen, device=dev).to(torch.bfloat16)
+    o_hf = torch.empty(HEADS, BATCH, 512, dtype=torch.bfloat16, device=dev)
+    ws = kimi.alloc_workspace(BATCH, HEADS, None, dev)
+    return dict(kvb=kvb, kvs=kvs, perm=perm, indptr=indptr, last=last, q=q, o_hf=o_hf, o=o_hf.permute(1, 0, 2),
+                ws=ws)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import kimi_b200 as kimi
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    # Two independent caches (2 x 210 MB > 126 MB L2), alternated step by step.
+    wl = [build_workload(torch, kimi, dev, seed=1000 * rank + s) for s in (1, 2)]
+    splits = kimi.num_kv_splits_for(BATCH, HEADS, None)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        w = wl[i & 1]
+        kimi.mla_decode_fwd(w["q"], w["kvb"], w["kvs"], w["o"], None, w["indptr"], w["perm"], w["last"],
+                            sm_scale=SM_SCALE, workspace=w["ws"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    with ClockSampler(dev.index) as clocks:
+        # ---- device-timed steps (inputs resident in HBM) ----
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms_total = max_over_ranks(e0.elapsed_time(e1))
+
+        # ---- per-call durations (events around every call) ----
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+        for i in range(args.steps):
+            w = wl[i & 1]
+            ev[2 * i].record(stream)
+            kimi.mla_decode_fwd(w["q"], w["kvb"], w["kvs"], w["o"], None, w["indptr"], w["perm"], w["last"],
+                                sm_scale=SM_SCALE, workspace=w["ws"])
+            ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+        call_ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)]
+
+        # ---- end to end through the public API with host buffers ----
+        q_host = [torch.empty_like(w["q"], device="cpu").pin_memory() for w in wl]
+        for qh, w in zip(q_host, wl):
+            qh.copy_(w["q"].cpu())
+        meta_host = [(w["indptr"].cpu().pin_memory(), w["perm"].cpu().pin_memory(), w["last"].cpu().pin_memory())
+                     for w in wl]
+        o_host = torch.empty(BATCH, HEADS, 512, dtype=torch.bfloat16).pin_memory()
+        dev_meta = [(torch.empty_like(w["indptr"]), torch.empty_like(w["perm"]), torch.empty_like(w["last"]))
+                    for w in wl]
+        h2d = q_host[0].numel() * 2 + sum(t.numel() * 4 for t in meta_host[0])
+        d2h = o_host.numel() * 2
+        barrier()
+        torch.cuda.synchronize()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for i in range(args.steps):
+            w, (ip_h, px_h, la_h), (ip_d, px_d, la_d) = wl[i & 1], meta_host[i & 1], dev_meta[i & 1]
+            w["q"].copy_(q_host[i & 1], non_blocking=True)
+            ip_d.copy_(ip_h, non_blocking=True)
+            px_d.copy_(px_h, non_blocking=True)
+            la_d.copy_(la_h, non_blocking=True)
+            kimi.mla_decode_fwd(w["q"], w["kvb"], w["kvs"], w["o"], None, ip_d, px_d, la_d,
+                                sm_scale=SM_SCALE, workspace=w["ws"])
+            o_host.copy_(w["o"], non_blocking=True)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e2.elapsed_time(e3))
+
+    # stage-1 / merge split of the call, from a single-kernel timing of the merge
+    red_ms = _time_reduce(torch, kimi, wl[0], splits, args.steps, stream) if splits > 1 else 0.0
+    nbytes = algorithmic_bytes()
+    ms_step = ms_total / args.steps
+    call_avg = sum(call_ms) / len(call_ms)
+    stage1_avg = max(call_avg - red_ms, 1e-6)
+    value_tbs = world * nbytes / (ms_step * 1e-3) / 1e12
+    e2e_tbs = world * nbytes / (e2e_ms / args.steps * 1e-3) / 1e12
+    peak, peak_kind = _peak_hbm()
+    achieved_gbs = nbytes / (stage1_avg * 1e-3) / 1e9
+    traffic = _traffic_summary()
+    clk = clocks.summary()
+    if rank != 0:
+        return None
+    cpu = cpu_baseline_sample() if world == 1 else None
+    line = {
+        "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "us_per_layer": round(ms_step * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded normal q and latents, cache written by the library's MXFP4 KV-append)",
+        "config": {"workload": WORKLOAD, "heads": HEADS, "batch_per_gpu": BATCH, "ctx": CTX, "page_size": PAGE,
+                   "num_kv_splits": splits, "sm_scale": "1/sqrt(192)",
+                   "algorithmic_bytes_per_gpu_step": nbytes,
+                   "l2": "inputs larger than L2: two independent 210 MB caches alternated between steps",
+                   "parallelism": f"dp{world} (batch-sharded, no collective in the step)"},
+        "e2e": {"value": round(e2e_tbs, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / args.steps, 5),
+                "path": "kimi_b200.mla_decode_fwd with q + page table copied from pinned host memory and o "
+                        "copied back every step"},
+        "gpu_launches": args.steps * (2 if splits > 1 else 1),
+        "kernels": {"stage1_ms": round(stage1_avg, 5), "merge_ms": round(red_ms, 5),
+                    "call_ms": round(call_avg, 5)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved_gbs / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS hbm_gbs)"
+                     if peak_kind == "measured" else "fallback",
+                     "kernel": "mla_decode stage 1 (split-K partial attention)",
+                     "traffic": None if traffic is None else traffic.get("dram_bytes_per_launch"),
+                     "traffic_source": None if traffic is None else traffic.get("source")},
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def _time_reduce(torch, kimi, w, splits, steps, stream):
+    """Average duration of the split-K merge alone on this workload's partials."""
+    ws = w["ws"]
+    rows = BATCH * splits * HEADS
+    po_bytes = ((rows * 512 * 4 + 255) // 256) * 256
+    po = ws[:rows * 512 * 4].view(torch.float32).view(BATCH, splits, HEADS, 512)
+    lse = ws[po_bytes:po_bytes + rows * 4].view(torch.float32).view(BATCH, splits, HEADS)
+    for _ in range(3):
+        kimi.mla_reduce(po, lse, w["o"])
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        kimi.mla_reduce(po, lse, w["o"])
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port of the reference torch path
+# ---------------------------------------------------------------------------
+def _cpu_sample_case(tokens: int, seed: int = 7):
+    import numpy as np
+
+    from oracle import mla as omla
+    from oracle import mxfp4 as omx
+    rng = np.random.default_rng(seed)
+    pages = tokens // PAGE
+    kv_c = omx.f32_to_bf16_bits(rng.standard_normal((pages * PAGE, 512), dtype=np.float32))
+    k_pe = omx.f32_to_bf16_bits(rng.standard_normal((pages * PAGE, 64), dtype=np.float32))
+    kvb, kvs = omla.empty_cache(pages)
+    omla.kv_append(kvb, kvs, kv_c, k_pe, np.arange(pages * PAGE))
+    q = omx.f32_to_bf16_bits(rng.standard_normal((1, HEADS, 576), dtype=np.float32))
+    return dict(q=q, kvb=kvb, kvs=kvs, indptr=np.array([0, pages], np.int32),
+                indices=rng.permutation(pages).astype(np.int32), last=np.array([PAGE], np.int32))
+
+
+def _cpu_decode(case):
+    from oracle import mla as omla
+    return omla.mla_decode(case["q"], case["kvb"], case["kvs"], case["indptr"], case["indices"], case["last"],
+                           SM_SCALE)
+
+
+def cpu_baseline_sample(target_s: float = 10.0):
+    """Time the oracle port of the reference's torch path on the host cores:
+    whole 8192-token sequences of the workload (64 heads), repeated for about
+    ``target_s`` seconds."""
+    case = _cpu_sample_case(CTX)
+    _cpu_decode(case)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        _cpu_decode(case)
+        n += 1
+        if time.perf_counter() - t0 >= target_s:
+            break
+    dt = time.perf_counter() - t0
+    nbytes = n * algorithmic_bytes(batch=1)
+    return {"value": round(nbytes / dt / 1e12, 6), "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} sequences of {CTX} tokens x {HEADS} heads (the numpy oracle of the reference torch "
+                      f"path: e2m1/e8m0 dequant + fp32 attention), {dt:.1f} s",
+            "us_per_layer_equiv": round(dt / n * BATCH * 1e6, 1)}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    tokens = 1024  # each step: one 1024-token slice of a sequence, 64 heads
+    case = _cpu_sample_case(tokens)
+    for _ in range(max(args.warmup, 1)):
+        _cpu_decode(case)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _cpu_decode(case)
+    dt = time.perf_counter() - t0
+    nbytes = tokens * TOKEN_BYTES_ALGO + HEADS * 576 * 2
+    val = nbytes * args.steps / dt / 1e12
+    ms_step_equiv = dt / args.steps * (algorithmic_bytes() / nbytes) * 1e3
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(val, 6), "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step_equiv, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded normal q and latents)",
+        "config": {"workload": WORKLOAD, "heads": HEADS, "batch_per_gpu": BATCH, "ctx": CTX, "page_size": PAGE,
+                   "step_sample": f"one {tokens}-token page-table slice of a sequence, {HEADS} heads",
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(val, 6), "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{args.steps} steps x {tokens} tokens x {HEADS} heads through the numpy "
+                                   "oracle of the reference torch path"},
+        "e2e": {"value": round(val, 6), "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

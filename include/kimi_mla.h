@@ -1,0 +1,175 @@
+/*
+ * kimi_mla.h -- C ABI of the B200 (sm_100a) MXFP4 absorbed-MLA decode path.
+ *
+ * Plain C: device pointers, sizes, element strides and a cudaStream_t passed
+ * as `void*`.  No C++ or torch types cross this boundary.  Every entry point
+ * is asynchronous on the given stream, allocates nothing, never synchronises
+ * the host and returns a status code:
+ *
+ *      0                  success (KIMI_OK)
+ *      negative           bad arguments, detected on the host before launch
+ *      positive           a CUDA runtime error from the launch (the cudaError_t
+ *                         value plus KIMI_ERR_CUDA_BASE)
+ *
+ * Reference interfaces replaced (paths inside the ianye23301/kimi tree):
+ *
+ *   kimi_mla_decode            aiter `mla_decode_fwd(q, kv_buffer, o, qo_indptr,
+ *                              kv_indptr, kv_indices, kv_last_page_len,
+ *                              max_seqlen_q, page_size, nhead_kv, sm_scale,
+ *                              logit_cap, num_kv_splits, ...)` as called at
+ *                              scripts/submission.py:115-133 and
+ *                              patches/atom-optimizations.patch:741-748, and
+ *                              the archive's `mla_decode_mxfp4`
+ *                              (archive/mla-mxfp4-dead-end/mla_decode_mxfp4_v5.py:313-376).
+ *                              Writes `o` in place; `o` may be the heads-first
+ *                              permuted view (patches/atom-optimizations.patch:261-289).
+ *   kimi_mla_decode_workspace_size
+ *                              the caller-owned split-K buffer of the reference
+ *                              (`attn_logits`, tests/test_triton_mla_decode.py:137-140,
+ *                              patches/atom-optimizations.patch:192-197).
+ *   kimi_mla_reduce            the split-K log-sum-exp merge `_mla_reduce`
+ *                              (archive/mla-mxfp4-dead-end/mla_decode_mxfp4_v5.py:264-306),
+ *                              aiter's stage-2 `_fwd_kernel_stage2_asm`.
+ *   kimi_mxfp4_kv_append       the KV-append cache writer
+ *                              `fused_qk_rope_concat_and_cache_mla(..., slot_mapping, ...)`
+ *                              (patches/atom-optimizations.patch:615-634) with the
+ *                              MXFP4 quantiser `_mxfp4_quant_inline`
+ *                              (archive/mla-mxfp4-dead-end/mla_decode_mxfp4_v5.py:18-75)
+ *                              or, with legacy_rule = 1, `_quantize_mxfp4_torch`
+ *                              (same file, :421-438).
+ *   kimi_mxfp4_quantize        row quantiser with the same two rules (aiter
+ *                              `dynamic_mxfp4_quant`, archive/mla-mxfp4-dead-end/mla_decode_mxfp4.py:139-156).
+ *
+ * Cache layout (one KV head, page size 64):
+ *   kv_buffer  uint8 [num_pages, 64, 384]: per token 256 bytes of e2m1 nibbles
+ *              of the 512-dim latent (element 2j in the low nibble of byte j)
+ *              followed by the 64-dim RoPE part as 128 bytes of bf16.
+ *   kv_scales  uint8 [num_pages, 64, 16]: per token 16 e8m0 scale bytes, one
+ *              per 32 latent elements; value = e2m1 * 2^(scale - 127).
+ * Both arrays are contiguous and 16-byte aligned.
+ */
+#ifndef KIMI_MLA_H_
+#define KIMI_MLA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KIMI_API __attribute__((visibility("default")))
+#else
+#define KIMI_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KIMI_MLA_KV_LORA_RANK 512
+#define KIMI_MLA_ROPE_DIM 64
+#define KIMI_MLA_QK_DIM 576
+#define KIMI_MLA_PAGE_SIZE 64
+#define KIMI_MLA_TOKEN_BYTES 384
+#define KIMI_MLA_SCALE_BYTES 16
+#define KIMI_MLA_MAX_SPLITS 64
+#define KIMI_MLA_MAX_HEADS 128
+
+enum {
+  KIMI_OK = 0,
+  KIMI_ERR_NULL_POINTER = -1,
+  KIMI_ERR_BAD_SHAPE = -2,
+  KIMI_ERR_BAD_STRIDE = -3,
+  KIMI_ERR_MISALIGNED = -4,
+  KIMI_ERR_WORKSPACE_TOO_SMALL = -5,
+  KIMI_ERR_UNSUPPORTED = -6,
+  KIMI_ERR_CUDA_BASE = 1000
+};
+
+/* Arguments of one decode call.  Element strides are in elements of the
+ * pointed-to type; the innermost dimension of q and o is contiguous. */
+typedef struct KimiMlaDecodeParams {
+  const void* q;              /* bf16 [batch, num_heads, 576] */
+  int64_t q_stride_b;
+  int64_t q_stride_h;
+  const void* kv_buffer;      /* uint8 [num_pages, 64, 384] */
+  const void* kv_scales;      /* uint8 [num_pages, 64, 16]  */
+  int64_t num_pages;
+  const int32_t* kv_indptr;   /* [batch + 1] page-table offsets */
+  const int32_t* kv_indices;  /* [kv_indptr[batch]] page ids    */
+  const int32_t* kv_last_page_len; /* [batch] tokens in the last page (1..64); NULL = full pages */
+  void* o;                    /* bf16 [batch, num_heads, 512], any (b, h) strides */
+  int64_t o_stride_b;
+  int64_t o_stride_h;
+  int32_t batch;
+  int32_t num_heads;          /* 1..128 */
+  int32_t num_kv_splits;      /* 1..64, or 0 = choose from batch and SM count */
+  float sm_scale;
+  float logit_cap;            /* must be 0 (no logit soft-capping on this path) */
+} KimiMlaDecodeParams;
+
+/* Bytes of caller-owned workspace one kimi_mla_decode call needs (split-K
+ * partial outputs and log-sum-exps).  num_kv_splits as in the params (0 =
+ * auto).  Returns 0 for invalid sizes. */
+KIMI_API size_t kimi_mla_decode_workspace_size(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
+
+/* The split count kimi_mla_decode uses for these sizes (resolves 0 = auto). */
+KIMI_API int32_t kimi_mla_decode_num_splits(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
+
+/* Absorbed-MLA decode, one query token per sequence, one KV head. */
+KIMI_API int kimi_mla_decode(const KimiMlaDecodeParams* params, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Split-K merge.  partial_o float32 [batch, num_splits, num_heads, 512]
+ * (each split normalised by its own softmax sum), partial_lse float32
+ * [batch, num_splits, num_heads] (natural-log log-sum-exp of the split's
+ * scaled scores; -inf for an empty split).  Writes bf16 o through strides. */
+typedef struct KimiMlaReduceParams {
+  const float* partial_o;
+  const float* partial_lse;
+  void* o;
+  int64_t o_stride_b;
+  int64_t o_stride_h;
+  int32_t batch;
+  int32_t num_heads;
+  int32_t num_splits;
+} KimiMlaReduceParams;
+
+KIMI_API int kimi_mla_reduce(const KimiMlaReduceParams* params, void* stream);
+
+/* Quantise kv_c (bf16 [num_tokens, 512]) to MXFP4 and write it, with k_pe
+ * (bf16 [num_tokens, 64]) copied verbatim, into the paged cache at flat slots
+ * slot_mapping[i] = page * 64 + row.  A negative slot skips its token; a slot
+ * >= num_pages * 64 is an error the kernel skips (the host cannot see device
+ * slot values without a sync).  legacy_rule: 0 = the in-kernel Triton rule,
+ * 1 = the reference's legacy torch rule. */
+typedef struct KimiKvAppendParams {
+  const void* kv_c;           /* bf16 [num_tokens, 512] */
+  int64_t kv_c_stride;
+  const void* k_pe;           /* bf16 [num_tokens, 64] */
+  int64_t k_pe_stride;
+  const int64_t* slot_mapping; /* [num_tokens] */
+  void* kv_buffer;            /* uint8 [num_pages, 64, 384] */
+  void* kv_scales;            /* uint8 [num_pages, 64, 16]  */
+  int64_t num_pages;
+  int32_t num_tokens;
+  int32_t legacy_rule;
+} KimiKvAppendParams;
+
+KIMI_API int kimi_mxfp4_kv_append(const KimiKvAppendParams* params, void* stream);
+
+/* Row quantiser: x bf16 [rows, cols] (row stride x_stride elements, cols a
+ * multiple of 32) -> nibbles uint8 [rows, cols/2] and scales uint8
+ * [rows, cols/32], both contiguous. */
+KIMI_API int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride,
+                        void* nibbles, void* scales, int32_t legacy_rule, void* stream);
+
+/* Human-readable text for a status code (static storage). */
+KIMI_API const char* kimi_status_string(int status);
+
+/* ABI version of this header (major * 100 + minor). */
+KIMI_API int kimi_abi_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* KIMI_MLA_H_ */

@@ -1,0 +1,126 @@
+"""ctypes binding of ``libkimi_mla.so`` (the C ABI declared in include/kimi_mla.h).
+
+The library is built in-tree by :mod:`kimi_b200.build`.  There is no other
+implementation behind these calls: if the library is missing, every call
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libkimi_mla.so")
+
+KIMI_OK = 0
+KIMI_ERR_CUDA_BASE = 1000
+
+# Symbols the header declares; tests check the library exports each one.
+EXPORTED_SYMBOLS = (
+    "kimi_abi_version",
+    "kimi_status_string",
+    "kimi_mla_decode_workspace_size",
+    "kimi_mla_decode_num_splits",
+    "kimi_mla_decode",
+    "kimi_mla_reduce",
+    "kimi_mxfp4_kv_append",
+    "kimi_mxfp4_quantize",
+)
+
+
+class KimiMlaDecodeParams(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("q_stride_b", ctypes.c_int64),
+        ("q_stride_h", ctypes.c_int64),
+        ("kv_buffer", ctypes.c_void_p),
+        ("kv_scales", ctypes.c_void_p),
+        ("num_pages", ctypes.c_int64),
+        ("kv_indptr", ctypes.c_void_p),
+        ("kv_indices", ctypes.c_void_p),
+        ("kv_last_page_len", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("o_stride_b", ctypes.c_int64),
+        ("o_stride_h", ctypes.c_int64),
+        ("batch", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("num_kv_splits", ctypes.c_int32),
+        ("sm_scale", ctypes.c_float),
+        ("logit_cap", ctypes.c_float),
+    ]
+
+
+class KimiMlaReduceParams(ctypes.Structure):
+    _fields_ = [
+        ("partial_o", ctypes.c_void_p),
+        ("partial_lse", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("o_stride_b", ctypes.c_int64),
+        ("o_stride_h", ctypes.c_int64),
+        ("batch", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("num_splits", ctypes.c_int32),
+    ]
+
+
+class KimiKvAppendParams(ctypes.Structure):
+    _fields_ = [
+        ("kv_c", ctypes.c_void_p),
+        ("kv_c_stride", ctypes.c_int64),
+        ("k_pe", ctypes.c_void_p),
+        ("k_pe_stride", ctypes.c_int64),
+        ("slot_mapping", ctypes.c_void_p),
+        ("kv_buffer", ctypes.c_void_p),
+        ("kv_scales", ctypes.c_void_p),
+        ("num_pages", ctypes.c_int64),
+        ("num_tokens", ctypes.c_int32),
+        ("legacy_rule", ctypes.c_int32),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once) and declare its signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m kimi_b200.build` "
+                "(this package has no CPU or Python fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+        lib.kimi_abi_version.restype = ctypes.c_int
+        lib.kimi_abi_version.argtypes = []
+        lib.kimi_status_string.restype = ctypes.c_char_p
+        lib.kimi_status_string.argtypes = [ctypes.c_int]
+        lib.kimi_mla_decode_workspace_size.restype = sz
+        lib.kimi_mla_decode_workspace_size.argtypes = [i32, i32, i32]
+        lib.kimi_mla_decode_num_splits.restype = i32
+        lib.kimi_mla_decode_num_splits.argtypes = [i32, i32, i32]
+        lib.kimi_mla_decode.restype = ctypes.c_int
+        lib.kimi_mla_decode.argtypes = [ctypes.POINTER(KimiMlaDecodeParams), vp, sz, vp]
+        lib.kimi_mla_reduce.restype = ctypes.c_int
+        lib.kimi_mla_reduce.argtypes = [ctypes.POINTER(KimiMlaReduceParams), vp]
+        lib.kimi_mxfp4_kv_append.restype = ctypes.c_int
+        lib.kimi_mxfp4_kv_append.argtypes = [ctypes.POINTER(KimiKvAppendParams), vp]
+        lib.kimi_mxfp4_quantize.restype = ctypes.c_int
+        lib.kimi_mxfp4_quantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, vp]
+        _lib = lib
+        return _lib
+
+
+def status_text(status: int) -> str:
+    return load().kimi_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != KIMI_OK:
+        kind = RuntimeError if status > 0 else ValueError
+        raise kind(f"{what} failed: {status_text(status)} (status {status})")

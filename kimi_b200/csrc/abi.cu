@@ -1,0 +1,208 @@
+// C ABI of the library (declared in include/kimi_mla.h): host-side argument
+// checks, workspace layout, split-count choice, and kernel launches.  No
+// allocation, no host synchronisation.
+#include <cmath>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "../../include/kimi_mla.h"
+#include "kernels.cuh"
+
+namespace {
+
+using kimi::kLatent;
+
+inline bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+inline int cuda_status(cudaError_t e) {
+  return e == cudaSuccess ? KIMI_OK : KIMI_ERR_CUDA_BASE + static_cast<int>(e);
+}
+
+int device_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+int resolve_splits(int32_t batch, int32_t num_heads, int32_t requested) {
+  if (requested > 0) return requested > KIMI_MLA_MAX_SPLITS ? KIMI_MLA_MAX_SPLITS : requested;
+  // Auto: about one CTA per SM over (sequence, split, head block), at most 32.
+  const int head_blocks = (num_heads + 63) / 64;
+  const long ctas = static_cast<long>(batch) * head_blocks;
+  if (ctas <= 0) return 1;
+  long s = (device_sm_count() + ctas / 2) / ctas;
+  if (s < 1) s = 1;
+  if (s > 32) s = 32;
+  return static_cast<int>(s);
+}
+
+size_t workspace_bytes_for(int64_t batch, int64_t heads, int64_t splits) {
+  if (splits <= 1) return 0;
+  const size_t rows = static_cast<size_t>(batch) * splits * heads;
+  size_t bytes = rows * kLatent * sizeof(float);
+  bytes = (bytes + 255) & ~static_cast<size_t>(255);
+  bytes += rows * sizeof(float);
+  return (bytes + 255) & ~static_cast<size_t>(255);
+}
+
+}  // namespace
+
+extern "C" {
+
+int kimi_abi_version(void) { return 100; }
+
+const char* kimi_status_string(int status) {
+  switch (status) {
+    case KIMI_OK: return "ok";
+    case KIMI_ERR_NULL_POINTER: return "null pointer argument";
+    case KIMI_ERR_BAD_SHAPE: return "unsupported or inconsistent shape";
+    case KIMI_ERR_BAD_STRIDE: return "unsupported stride";
+    case KIMI_ERR_MISALIGNED: return "pointer or stride not aligned as required";
+    case KIMI_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case KIMI_ERR_UNSUPPORTED: return "unsupported option";
+    default: break;
+  }
+  if (status >= KIMI_ERR_CUDA_BASE) return cudaGetErrorString(static_cast<cudaError_t>(status - KIMI_ERR_CUDA_BASE));
+  return "unknown status";
+}
+
+int32_t kimi_mla_decode_num_splits(int32_t batch, int32_t num_heads, int32_t num_kv_splits) {
+  if (batch < 0 || num_heads < 1 || num_heads > KIMI_MLA_MAX_HEADS || num_kv_splits < 0) return 0;
+  return resolve_splits(batch, num_heads, num_kv_splits);
+}
+
+size_t kimi_mla_decode_workspace_size(int32_t batch, int32_t num_heads, int32_t num_kv_splits) {
+  if (batch < 0 || num_heads < 1 || num_heads > KIMI_MLA_MAX_HEADS || num_kv_splits < 0) return 0;
+  return workspace_bytes_for(batch, num_heads, resolve_splits(batch, num_heads, num_kv_splits));
+}
+
+int kimi_mla_decode(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!p) return KIMI_ERR_NULL_POINTER;
+  if (p->batch < 0 || p->num_heads < 1 || p->num_heads > KIMI_MLA_MAX_HEADS || p->num_kv_splits < 0 ||
+      p->num_kv_splits > KIMI_MLA_MAX_SPLITS || p->num_pages < 0)
+    return KIMI_ERR_BAD_SHAPE;
+  if (p->logit_cap != 0.0f) return KIMI_ERR_UNSUPPORTED;
+  if (!std::isfinite(p->sm_scale)) return KIMI_ERR_BAD_SHAPE;
+  if (p->batch == 0) return KIMI_OK;
+  if (!p->q || !p->kv_buffer || !p->kv_scales || !p->kv_indptr || !p->kv_indices || !p->o)
+    return KIMI_ERR_NULL_POINTER;
+  if (p->q_stride_b % 8 || p->q_stride_h % 8 || p->o_stride_b % 4 || p->o_stride_h % 4)
+    return KIMI_ERR_BAD_STRIDE;
+  if (!aligned(p->q, 16) || !aligned(p->kv_buffer, 16) || !aligned(p->kv_scales, 16) || !aligned(p->o, 8))
+    return KIMI_ERR_MISALIGNED;
+  const int splits = resolve_splits(p->batch, p->num_heads, p->num_kv_splits);
+  const size_t need = workspace_bytes_for(p->batch, p->num_heads, splits);
+  if (need > 0) {
+    if (!workspace || workspace_bytes < need) return KIMI_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(workspace, 256)) return KIMI_ERR_MISALIGNED;
+  }
+  const size_t rows = static_cast<size_t>(p->batch) * splits * p->num_heads;
+  const size_t po_bytes = (rows * kLatent * sizeof(float) + 255) & ~static_cast<size_t>(255);
+
+  kimi::DecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(p->q);
+  a.q_stride_b = p->q_stride_b;
+  a.q_stride_h = p->q_stride_h;
+  a.kv_buffer = static_cast<const uint8_t*>(p->kv_buffer);
+  a.kv_scales = static_cast<const uint8_t*>(p->kv_scales);
+  a.num_pages = p->num_pages;
+  a.kv_indptr = p->kv_indptr;
+  a.kv_indices = p->kv_indices;
+  a.kv_last_page_len = p->kv_last_page_len;
+  a.o = static_cast<__nv_bfloat16*>(p->o);
+  a.o_stride_b = p->o_stride_b;
+  a.o_stride_h = p->o_stride_h;
+  a.partial_o = need ? static_cast<float*>(workspace) : nullptr;
+  a.partial_lse = need ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + po_bytes) : nullptr;
+  a.batch = p->batch;
+  a.num_heads = p->num_heads;
+  a.num_splits = splits;
+  a.sm_scale = p->sm_scale;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = kimi::launch_decode_mma(a, s);
+  if (e != cudaSuccess || splits == 1) return cuda_status(e);
+
+  kimi::ReduceArgs r;
+  r.partial_o = a.partial_o;
+  r.partial_lse = a.partial_lse;
+  r.o = a.o;
+  r.o_stride_b = a.o_stride_b;
+  r.o_stride_h = a.o_stride_h;
+  r.batch = a.batch;
+  r.num_heads = a.num_heads;
+  r.num_splits = splits;
+  return cuda_status(kimi::launch_reduce(r, s));
+}
+
+int kimi_mla_reduce(const KimiMlaReduceParams* p, void* stream) {
+  if (!p) return KIMI_ERR_NULL_POINTER;
+  if (p->batch < 0 || p->num_heads < 1 || p->num_heads > KIMI_MLA_MAX_HEADS || p->num_splits < 1 ||
+      p->num_splits > KIMI_MLA_MAX_SPLITS)
+    return KIMI_ERR_BAD_SHAPE;
+  if (p->batch == 0) return KIMI_OK;
+  if (!p->partial_o || !p->partial_lse || !p->o) return KIMI_ERR_NULL_POINTER;
+  if (p->o_stride_b % 4 || p->o_stride_h % 4) return KIMI_ERR_BAD_STRIDE;
+  if (!aligned(p->partial_o, 16) || !aligned(p->partial_lse, 4) || !aligned(p->o, 8)) return KIMI_ERR_MISALIGNED;
+  kimi::ReduceArgs r;
+  r.partial_o = p->partial_o;
+  r.partial_lse = p->partial_lse;
+  r.o = static_cast<__nv_bfloat16*>(p->o);
+  r.o_stride_b = p->o_stride_b;
+  r.o_stride_h = p->o_stride_h;
+  r.batch = p->batch;
+  r.num_heads = p->num_heads;
+  r.num_splits = p->num_splits;
+  return cuda_status(kimi::launch_reduce(r, static_cast<cudaStream_t>(stream)));
+}
+
+int kimi_mxfp4_kv_append(const KimiKvAppendParams* p, void* stream) {
+  if (!p) return KIMI_ERR_NULL_POINTER;
+  if (p->num_tokens < 0 || p->num_pages < 0) return KIMI_ERR_BAD_SHAPE;
+  if (p->legacy_rule != 0 && p->legacy_rule != 1) return KIMI_ERR_UNSUPPORTED;
+  if (p->num_tokens == 0) return KIMI_OK;
+  if (!p->kv_c || !p->k_pe || !p->slot_mapping || !p->kv_buffer || !p->kv_scales) return KIMI_ERR_NULL_POINTER;
+  if (p->kv_c_stride % 8 || p->k_pe_stride % 8 || p->kv_c_stride < kLatent || p->k_pe_stride < 64)
+    return KIMI_ERR_BAD_STRIDE;
+  if (!aligned(p->kv_c, 16) || !aligned(p->k_pe, 16) || !aligned(p->kv_buffer, 16) || !aligned(p->slot_mapping, 8))
+    return KIMI_ERR_MISALIGNED;
+  kimi::KvAppendArgs a;
+  a.kv_c = static_cast<const __nv_bfloat16*>(p->kv_c);
+  a.kv_c_stride = p->kv_c_stride;
+  a.k_pe = static_cast<const __nv_bfloat16*>(p->k_pe);
+  a.k_pe_stride = p->k_pe_stride;
+  a.slot_mapping = p->slot_mapping;
+  a.kv_buffer = static_cast<uint8_t*>(p->kv_buffer);
+  a.kv_scales = static_cast<uint8_t*>(p->kv_scales);
+  a.num_pages = p->num_pages;
+  a.num_tokens = p->num_tokens;
+  a.legacy_rule = p->legacy_rule;
+  return cuda_status(kimi::launch_kv_append(a, static_cast<cudaStream_t>(stream)));
+}
+
+int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,
+                        int32_t legacy_rule, void* stream) {
+  if (rows < 0 || cols < 0 || cols % 32) return KIMI_ERR_BAD_SHAPE;
+  if (legacy_rule != 0 && legacy_rule != 1) return KIMI_ERR_UNSUPPORTED;
+  if (rows == 0 || cols == 0) return KIMI_OK;
+  if (!x || !nibbles || !scales) return KIMI_ERR_NULL_POINTER;
+  if (x_stride % 8 || x_stride < cols) return KIMI_ERR_BAD_STRIDE;
+  if (!aligned(x, 16) || !aligned(nibbles, 16)) return KIMI_ERR_MISALIGNED;
+  kimi::QuantizeArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.rows = rows;
+  a.cols = cols;
+  a.x_stride = x_stride;
+  a.nibbles = static_cast<uint8_t*>(nibbles);
+  a.scales = static_cast<uint8_t*>(scales);
+  a.legacy_rule = legacy_rule;
+  return cuda_status(kimi::launch_quantize_rows(a, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,237 @@
+"""Host-side operator API of the MXFP4 MLA decode path.
+
+Mirrors the reference's operator interface (paths inside ianye23301/kimi):
+
+* :func:`mla_decode_fwd` -- aiter ``mla_decode_fwd(q, kv_buffer, o, qo_indptr,
+  kv_indptr, kv_indices, kv_last_page_len, max_seqlen_q, page_size, nhead_kv,
+  sm_scale, logit_cap, num_kv_splits, ...)`` as called at
+  scripts/submission.py:115-133 and patches/atom-optimizations.patch:741-748,
+  with the MXFP4 cache's scale tensor ``kv_scales`` next to ``kv_buffer``.
+  Writes ``o`` in place on the current stream (``o`` may be the heads-first
+  view ``o_hf.permute(1, 0, 2)``, patches/atom-optimizations.patch:261-289).
+* :func:`mxfp4_kv_append` -- the cache writer
+  ``fused_qk_rope_concat_and_cache_mla(..., slot_mapping, ...)``
+  (patches/atom-optimizations.patch:615-634) with the MXFP4 quantiser.
+* :func:`mxfp4_quantize` -- aiter ``dynamic_mxfp4_quant``
+  (archive/mla-mxfp4-dead-end/mla_decode_mxfp4.py:139-156).
+* :func:`mla_reduce` -- the split-K merge ``_mla_reduce``
+  (archive/mla-mxfp4-dead-end/mla_decode_mxfp4_v5.py:264-306).
+
+Errors are Python exceptions (``ValueError`` for bad arguments, as the
+reference's asserts, ``RuntimeError`` for CUDA failures).  Every call runs the
+CUDA kernels of ``libkimi_mla.so``; there is no other path.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+KV_LORA_RANK = 512
+ROPE_DIM = 64
+QK_DIM = KV_LORA_RANK + ROPE_DIM
+PAGE_SIZE = 64
+TOKEN_BYTES = 384
+SCALE_BYTES = 16
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    if dev.type != "cuda":
+        raise ValueError("kimi_b200 kernels run on CUDA tensors only")
+    for t in tensors:
+        if t is not None and t.device != dev:
+            raise ValueError("all tensors must be on the same CUDA device")
+    return dev
+
+
+def _cache_views(kv_buffer: torch.Tensor, kv_scales: torch.Tensor):
+    """Accept [pages, 64, 384] / [pages, 64, 1, 384] (and the same for scales)."""
+    if kv_buffer.dtype != torch.uint8 or kv_scales.dtype != torch.uint8:
+        raise ValueError("kv_buffer and kv_scales must be uint8")
+    if not kv_buffer.is_contiguous() or not kv_scales.is_contiguous():
+        raise ValueError("kv_buffer and kv_scales must be contiguous")
+    if kv_buffer.numel() % (PAGE_SIZE * TOKEN_BYTES) or kv_buffer.shape[-1] != TOKEN_BYTES:
+        raise ValueError(f"kv_buffer must be [num_pages, {PAGE_SIZE}, {TOKEN_BYTES}] uint8")
+    num_pages = kv_buffer.numel() // (PAGE_SIZE * TOKEN_BYTES)
+    if kv_scales.numel() != num_pages * PAGE_SIZE * SCALE_BYTES or kv_scales.shape[-1] != SCALE_BYTES:
+        raise ValueError(f"kv_scales must be [num_pages, {PAGE_SIZE}, {SCALE_BYTES}] uint8")
+    return num_pages
+
+
+def alloc_mxfp4_cache(num_pages: int, device, zero: bool = True):
+    """A paged MXFP4 latent cache: ``(kv_buffer [P, 64, 384] u8, kv_scales [P, 64, 16] u8)``."""
+    make = torch.zeros if zero else torch.empty
+    return (make(num_pages, PAGE_SIZE, TOKEN_BYTES, dtype=torch.uint8, device=device),
+            make(num_pages, PAGE_SIZE, SCALE_BYTES, dtype=torch.uint8, device=device))
+
+
+def num_kv_splits_for(batch: int, num_heads: int, num_kv_splits: int | None = None) -> int:
+    """The split count the decode uses (``None``/0 = automatic)."""
+    return int(_lib.load().kimi_mla_decode_num_splits(batch, num_heads, int(num_kv_splits or 0)))
+
+
+def workspace_bytes(batch: int, num_heads: int, num_kv_splits: int | None = None) -> int:
+    return int(_lib.load().kimi_mla_decode_workspace_size(batch, num_heads, int(num_kv_splits or 0)))
+
+
+def alloc_workspace(batch: int, num_heads: int, num_kv_splits: int | None, device) -> torch.Tensor:
+    """Preallocate the split-K workspace (for CUDA-graph capture: allocate once,
+    pass it to every :func:`mla_decode_fwd` call of that shape)."""
+    n = workspace_bytes(batch, num_heads, num_kv_splits)
+    return torch.empty(max(n, 256), dtype=torch.uint8, device=device)
+
+
+_ws_cache: dict = {}
+
+
+def _default_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    key = (device.type, device.index)
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
+
+
+def mla_decode_fwd(q: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Tensor, o: torch.Tensor,
+                   qo_indptr: torch.Tensor | None, kv_indptr: torch.Tensor, kv_indices: torch.Tensor,
+                   kv_last_page_len: torch.Tensor | None, max_seqlen_q: int = 1, page_size: int = PAGE_SIZE,
+                   nhead_kv: int = 1, sm_scale: float | None = None, logit_cap: float = 0.0,
+                   num_kv_splits: int | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Absorbed-MLA decode over the paged MXFP4 latent cache; writes ``o``.
+
+    q            bf16 [batch, num_heads, 576] (rows may be strided; last dim contiguous)
+    kv_buffer    uint8 [num_pages, 64, 384] (nibbles of the 512-dim latent, then bf16 RoPE)
+    kv_scales    uint8 [num_pages, 64, 16]  (e8m0, one per 32 latent elements)
+    o            bf16 [batch, num_heads, 512], any (batch, head) strides
+    kv_indptr    int32 [batch + 1] page offsets; kv_indices int32 page ids;
+    kv_last_page_len int32 [batch] tokens in each last page (None = full pages)
+    sm_scale     softmax scale (default 1/sqrt(576))
+    num_kv_splits split-K count (None = automatic); workspace optional uint8
+                 buffer of at least :func:`workspace_bytes`
+    """
+    dev = _require_cuda(q, kv_buffer, kv_scales, o, kv_indptr, kv_indices)
+    if max_seqlen_q != 1:
+        raise ValueError("mla_decode_fwd supports one query token per sequence (max_seqlen_q == 1)")
+    if page_size != PAGE_SIZE:
+        raise ValueError(f"page_size must be {PAGE_SIZE}")
+    if nhead_kv != 1:
+        raise ValueError("MLA has one latent KV head (nhead_kv == 1)")
+    if q.dtype != torch.bfloat16 or o.dtype != torch.bfloat16:
+        raise ValueError("q and o must be bfloat16")
+    if q.dim() != 3 or q.shape[2] != QK_DIM or q.stride(2) != 1:
+        raise ValueError(f"q must be [batch, heads, {QK_DIM}] with a contiguous last dim")
+    batch, heads = q.shape[0], q.shape[1]
+    if o.dim() != 3 or tuple(o.shape) != (batch, heads, KV_LORA_RANK) or o.stride(2) != 1:
+        raise ValueError(f"o must be [batch, heads, {KV_LORA_RANK}] with a contiguous last dim")
+    if qo_indptr is not None and qo_indptr.numel() != batch + 1:
+        raise ValueError("qo_indptr must have batch + 1 entries")
+    for name, t in (("kv_indptr", kv_indptr), ("kv_indices", kv_indices), ("kv_last_page_len", kv_last_page_len)):
+        if t is not None and (t.dtype != torch.int32 or not t.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous int32 tensor")
+    if kv_indptr.numel() != batch + 1:
+        raise ValueError("kv_indptr must have batch + 1 entries")
+    if kv_last_page_len is not None and kv_last_page_len.numel() != batch:
+        raise ValueError("kv_last_page_len must have batch entries")
+    num_pages = _cache_views(kv_buffer, kv_scales)
+    scale = (1.0 / math.sqrt(QK_DIM)) if sm_scale is None else float(sm_scale)
+    lib = _lib.load()
+    splits_req = int(num_kv_splits or 0)
+    need = int(lib.kimi_mla_decode_workspace_size(batch, heads, splits_req))
+    if need:
+        if workspace is None:
+            workspace = _default_workspace(need, dev)
+        elif workspace.device != dev or workspace.numel() * workspace.element_size() < need:
+            raise ValueError(f"workspace must hold at least {need} bytes on {dev}")
+    p = _lib.KimiMlaDecodeParams(
+        q=q.data_ptr(), q_stride_b=q.stride(0), q_stride_h=q.stride(1),
+        kv_buffer=kv_buffer.data_ptr(), kv_scales=kv_scales.data_ptr(), num_pages=num_pages,
+        kv_indptr=kv_indptr.data_ptr(), kv_indices=kv_indices.data_ptr() if kv_indices.numel() else None,
+        kv_last_page_len=_ptr(kv_last_page_len),
+        o=o.data_ptr(), o_stride_b=o.stride(0), o_stride_h=o.stride(1),
+        batch=batch, num_heads=heads, num_kv_splits=splits_req,
+        sm_scale=scale, logit_cap=float(logit_cap))
+    if p.kv_indices is None and batch:
+        # an all-empty batch still needs a valid pointer; the kernel never reads past kv_indptr
+        p.kv_indices = kv_indptr.data_ptr()
+    ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
+    ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
+    with torch.cuda.device(dev):
+        status = lib.kimi_mla_decode(ctypes.byref(p), ws_ptr, ws_bytes, _stream_handle(dev))
+    _lib.check(status, "kimi_mla_decode")
+    return o
+
+
+def mla_reduce(partial_o: torch.Tensor, partial_lse: torch.Tensor, o: torch.Tensor) -> torch.Tensor:
+    """Merge split partials: partial_o f32 [B, S, H, 512], partial_lse f32 [B, S, H]
+    (natural log, -inf = empty split) -> bf16 ``o`` [B, H, 512] (any strides)."""
+    dev = _require_cuda(partial_o, partial_lse, o)
+    b, s, h, d = partial_o.shape
+    if d != KV_LORA_RANK or tuple(partial_lse.shape) != (b, s, h):
+        raise ValueError("partial_o must be [B, S, H, 512] and partial_lse [B, S, H]")
+    if partial_o.dtype != torch.float32 or partial_lse.dtype != torch.float32:
+        raise ValueError("partials must be float32")
+    if not partial_o.is_contiguous() or not partial_lse.is_contiguous():
+        raise ValueError("partials must be contiguous")
+    if o.dtype != torch.bfloat16 or tuple(o.shape) != (b, h, KV_LORA_RANK) or o.stride(2) != 1:
+        raise ValueError("o must be bf16 [B, H, 512] with a contiguous last dim")
+    p = _lib.KimiMlaReduceParams(partial_o=partial_o.data_ptr(), partial_lse=partial_lse.data_ptr(),
+                                 o=o.data_ptr(), o_stride_b=o.stride(0), o_stride_h=o.stride(1),
+                                 batch=b, num_heads=h, num_splits=s)
+    with torch.cuda.device(dev):
+        status = _lib.load().kimi_mla_reduce(ctypes.byref(p), _stream_handle(dev))
+    _lib.check(status, "kimi_mla_reduce")
+    return o
+
+
+def mxfp4_kv_append(kv_c: torch.Tensor, k_pe: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Tensor,
+                    slot_mapping: torch.Tensor, legacy_rule: bool = False) -> None:
+    """Quantise ``kv_c`` (bf16 [n, 512]) to MXFP4 and write it, with ``k_pe``
+    (bf16 [n, 64]), into the paged cache at ``slot_mapping`` (int64 [n],
+    page * 64 + row; negative = skip)."""
+    dev = _require_cuda(kv_c, k_pe, kv_buffer, kv_scales, slot_mapping)
+    num_pages = _cache_views(kv_buffer, kv_scales)
+    if kv_c.dtype != torch.bfloat16 or k_pe.dtype != torch.bfloat16:
+        raise ValueError("kv_c and k_pe must be bfloat16")
+    if kv_c.dim() != 2 or kv_c.shape[1] != KV_LORA_RANK or kv_c.stride(1) != 1:
+        raise ValueError("kv_c must be [n, 512] with a contiguous last dim")
+    if k_pe.dim() != 2 or k_pe.shape[1] != ROPE_DIM or k_pe.stride(1) != 1 or k_pe.shape[0] != kv_c.shape[0]:
+        raise ValueError("k_pe must be [n, 64] with a contiguous last dim")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() != kv_c.shape[0] or not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be a contiguous int64 tensor with n entries")
+    p = _lib.KimiKvAppendParams(kv_c=kv_c.data_ptr(), kv_c_stride=kv_c.stride(0), k_pe=k_pe.data_ptr(),
+                                k_pe_stride=k_pe.stride(0), slot_mapping=slot_mapping.data_ptr(),
+                                kv_buffer=kv_buffer.data_ptr(), kv_scales=kv_scales.data_ptr(),
+                                num_pages=num_pages, num_tokens=kv_c.shape[0], legacy_rule=int(bool(legacy_rule)))
+    with torch.cuda.device(dev):
+        status = _lib.load().kimi_mxfp4_kv_append(ctypes.byref(p), _stream_handle(dev))
+    _lib.check(status, "kimi_mxfp4_kv_append")
+
+
+def mxfp4_quantize(x: torch.Tensor, legacy_rule: bool = False):
+    """bf16 [rows, cols] (cols % 32 == 0) -> (nibbles u8 [rows, cols/2], scales u8 [rows, cols/32])."""
+    dev = _require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be a bf16 [rows, cols] tensor with a contiguous last dim")
+    rows, cols = x.shape
+    if cols % 32:
+        raise ValueError("cols must be a multiple of 32")
+    nib = torch.empty(rows, cols // 2, dtype=torch.uint8, device=dev)
+    sc = torch.empty(rows, cols // 32, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        status = _lib.load().kimi_mxfp4_quantize(x.data_ptr(), rows, cols, x.stride(0), nib.data_ptr(),
+                                                 sc.data_ptr(), int(bool(legacy_rule)), _stream_handle(dev))
+    _lib.check(status, "kimi_mxfp4_quantize")
+    return nib, sc

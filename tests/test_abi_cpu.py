@@ -1,0 +1,101 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol the header
+declares, and rejects bad arguments on the host before any launch."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from kimi_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "kimi_mla.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"KIMI_API\s+[\w\s\*]*?\b(kimi_\w+)\s*\(", text)))
+
+
+def test_header_declarations_match_binding_list():
+    assert _declared_functions() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.kimi_abi_version() == 100
+    assert _lib.status_text(0) == "ok"
+    assert "workspace" in _lib.status_text(-5)
+    assert _lib.status_text(-12345) == "unknown status"
+
+
+def test_workspace_size_arithmetic():
+    lib = _lib.load()
+    # explicit splits: partial O (B*S*H*512 f32) + LSE (B*S*H f32), each rounded to 256 B
+    b, h, s = 64, 64, 4
+    rows = b * s * h
+    expect = ((rows * 512 * 4 + 255) // 256) * 256 + ((rows * 4 + 255) // 256) * 256
+    assert lib.kimi_mla_decode_workspace_size(b, h, s) == expect
+    assert lib.kimi_mla_decode_workspace_size(b, h, 1) == 0  # single split writes o directly
+    assert lib.kimi_mla_decode_workspace_size(b, 0, 4) == 0  # invalid
+    assert lib.kimi_mla_decode_num_splits(b, h, 7) == 7
+    assert lib.kimi_mla_decode_num_splits(b, h, 999) == 64
+    assert 1 <= lib.kimi_mla_decode_num_splits(2, 16, 0) <= 32
+
+
+def test_decode_rejects_bad_arguments_on_host():
+    lib = _lib.load()
+    assert lib.kimi_mla_decode(None, None, 0, None) == -1
+    p = _lib.KimiMlaDecodeParams(batch=2, num_heads=0, num_kv_splits=1, sm_scale=0.1)
+    assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -2
+    p = _lib.KimiMlaDecodeParams(batch=2, num_heads=16, num_kv_splits=1, sm_scale=0.1, logit_cap=30.0)
+    assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -6
+    p = _lib.KimiMlaDecodeParams(batch=2, num_heads=16, num_kv_splits=1, sm_scale=0.1)
+    assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -1  # null tensors
+    # misaligned q pointer (the library never dereferences host-side checks' inputs)
+    p = _lib.KimiMlaDecodeParams(q=0x1002, q_stride_b=16 * 576, q_stride_h=576, kv_buffer=0x1000,
+                                 kv_scales=0x2000, num_pages=1, kv_indptr=0x3000, kv_indices=0x4000,
+                                 o=0x5000, o_stride_b=16 * 512, o_stride_h=512, batch=2, num_heads=16,
+                                 num_kv_splits=1, sm_scale=0.1)
+    assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -4
+    p.q = 0x1000
+    p.q_stride_h = 577
+    assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -3
+    p.q_stride_h = 576
+    p.num_kv_splits = 4
+    assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -5  # no workspace for 4 splits
+    # batch 0 is a no-op
+    p0 = _lib.KimiMlaDecodeParams(batch=0, num_heads=16, num_kv_splits=1, sm_scale=0.1)
+    assert lib.kimi_mla_decode(ctypes.byref(p0), None, 0, None) == 0
+
+
+def test_append_and_quantize_reject_bad_arguments_on_host():
+    lib = _lib.load()
+    assert lib.kimi_mxfp4_kv_append(None, None) == -1
+    p = _lib.KimiKvAppendParams(num_tokens=4, num_pages=1, legacy_rule=2)
+    assert lib.kimi_mxfp4_kv_append(ctypes.byref(p), None) == -6
+    p = _lib.KimiKvAppendParams(kv_c=0x1000, kv_c_stride=500, k_pe=0x2000, k_pe_stride=64, slot_mapping=0x3000,
+                                kv_buffer=0x4000, kv_scales=0x5000, num_pages=1, num_tokens=4)
+    assert lib.kimi_mxfp4_kv_append(ctypes.byref(p), None) == -3
+    assert lib.kimi_mxfp4_quantize(None, 4, 48, 48, None, None, 0, None) == -2   # cols % 32
+    assert lib.kimi_mxfp4_quantize(None, 4, 64, 64, None, None, 0, None) == -1
+    assert lib.kimi_mxfp4_quantize(0x1000, 0, 64, 64, 0x2000, 0x3000, 0, None) == 0  # empty
+
+
+def test_python_wrappers_reject_cpu_tensors():
+    import torch
+
+    import kimi_b200
+
+    q = torch.zeros(1, 16, 576, dtype=torch.bfloat16)
+    kvb, kvs = torch.zeros(1, 64, 384, dtype=torch.uint8), torch.zeros(1, 64, 16, dtype=torch.uint8)
+    o = torch.zeros(1, 16, 512, dtype=torch.bfloat16)
+    ip = torch.tensor([0, 1], dtype=torch.int32)
+    with pytest.raises(ValueError):
+        kimi_b200.mla_decode_fwd(q, kvb, kvs, o, None, ip, ip[:1], None)

@@ -242,7 +242,7 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.summary()
     if rank != 0:
         return None
-    cpu = cpu_baseline_sample() if world == 1 else None
+    cpu = cpu_baseline_sample(args.cpu_baseline_seconds) if (world == 1 and args.cpu_baseline_seconds > 0) else None
     line = {
         "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "us_per_layer": round(ms_step * 1e3, 2),
@@ -372,6 +372,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
+                    help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

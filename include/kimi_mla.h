@@ -72,6 +72,7 @@ extern "C" {
 #define KIMI_MLA_SCALE_BYTES 16
 #define KIMI_MLA_MAX_SPLITS 64
 #define KIMI_MLA_MAX_HEADS 128
+#define KIMI_MLA_STATIC_WORKSPACE_BYTES 33554432u /* 32 MiB, see kimi_mla_decode_static_workspace */
 
 enum {
   KIMI_OK = 0,
@@ -81,6 +82,7 @@ enum {
   KIMI_ERR_MISALIGNED = -4,
   KIMI_ERR_WORKSPACE_TOO_SMALL = -5,
   KIMI_ERR_UNSUPPORTED = -6,
+  KIMI_ERR_STATIC_WORKSPACE_LIMIT = -7,
   KIMI_ERR_CUDA_BASE = 1000
 };
 
@@ -117,6 +119,24 @@ KIMI_API int32_t kimi_mla_decode_num_splits(int32_t batch, int32_t num_heads, in
 /* Absorbed-MLA decode, one query token per sequence, one KV head. */
 KIMI_API int kimi_mla_decode(const KimiMlaDecodeParams* params, void* workspace, size_t workspace_bytes,
                     void* stream);
+
+/* Same decode as kimi_mla_decode, for callers that cannot allocate device
+ * memory.  No counterpart in the reference: aiter and the archive kernels
+ * always take (or allocate) their split-K buffers.  Callers such as a
+ * foreign-language binding holding only the pointers an engine handed it, or
+ * an engine that reserved all free HBM up front, have no way to obtain the
+ * workspace kimi_mla_decode needs; this call takes it from a 32 MiB array
+ * compiled into the library instead (KIMI_MLA_STATIC_WORKSPACE_BYTES, held on
+ * every GPU that loads the library until exit) and allocates nothing.
+ *  - Returns KIMI_ERR_STATIC_WORKSPACE_LIMIT, launching nothing, when
+ *    kimi_mla_decode_workspace_size() for these sizes exceeds 32 MiB.
+ *  - All calls on a device share the array and it keeps the last call's
+ *    contents; calls that overlap on the GPU race, so order them on one
+ *    stream.  Nothing in it needs clearing between calls.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before any stream capture begins. */
+KIMI_API int kimi_mla_decode_static_workspace(const KimiMlaDecodeParams* params, void* stream);
 
 /* Split-K merge.  partial_o float32 [batch, num_splits, num_heads, 512]
  * (each split normalised by its own softmax sum), partial_lse float32

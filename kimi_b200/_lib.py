@@ -25,6 +25,7 @@ EXPORTED_SYMBOLS = (
     "kimi_mla_reduce",
     "kimi_mxfp4_kv_append",
     "kimi_mxfp4_quantize",
+    "kimi_mla_decode_static_workspace",
 )
 
 
@@ -110,6 +111,8 @@ def load() -> ctypes.CDLL:
         lib.kimi_mla_reduce.argtypes = [ctypes.POINTER(KimiMlaReduceParams), vp]
         lib.kimi_mxfp4_kv_append.restype = ctypes.c_int
         lib.kimi_mxfp4_kv_append.argtypes = [ctypes.POINTER(KimiKvAppendParams), vp]
+        lib.kimi_mla_decode_static_workspace.restype = ctypes.c_int
+        lib.kimi_mla_decode_static_workspace.argtypes = [ctypes.POINTER(KimiMlaDecodeParams), vp]
         lib.kimi_mxfp4_quantize.restype = ctypes.c_int
         lib.kimi_mxfp4_quantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, vp]
         _lib = lib

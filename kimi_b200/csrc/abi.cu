@@ -67,6 +67,8 @@ const char* kimi_status_string(int status) {
     case KIMI_ERR_MISALIGNED: return "pointer or stride not aligned as required";
     case KIMI_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
     case KIMI_ERR_UNSUPPORTED: return "unsupported option";
+    case KIMI_ERR_STATIC_WORKSPACE_LIMIT:
+      return "split-K partials exceed the library's 32 MiB static workspace (use kimi_mla_decode with a caller workspace)";
     default: break;
   }
   if (status >= KIMI_ERR_CUDA_BASE) return cudaGetErrorString(static_cast<cudaError_t>(status - KIMI_ERR_CUDA_BASE));

@@ -3,6 +3,8 @@
 // allocation, no host synchronisation.
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 
 #include <cuda_runtime.h>
 
@@ -41,6 +43,17 @@ int resolve_splits(int32_t batch, int32_t num_heads, int32_t requested) {
   if (s < 1) s = 1;
   if (s > 32) s = 32;
   return static_cast<int>(s);
+}
+
+// KIMI_MLA_DECODE_KERNEL=mma selects the warp-level mma.sync decode (kept for
+// comparison); the default is the tcgen05 kernel.
+bool use_warp_mma_kernel() {
+  static int choice = -1;
+  if (choice < 0) {
+    const char* v = std::getenv("KIMI_MLA_DECODE_KERNEL");
+    choice = (v && std::strcmp(v, "mma") == 0) ? 1 : 0;
+  }
+  return choice == 1;
 }
 
 size_t workspace_bytes_for(int64_t batch, int64_t heads, int64_t splits) {
@@ -127,8 +140,9 @@ int kimi_mla_decode(const KimiMlaDecodeParams* p, void* workspace, size_t worksp
   a.num_heads = p->num_heads;
   a.num_splits = splits;
   a.sm_scale = p->sm_scale;
+  a.status = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = kimi::launch_decode_mma(a, s);
+  cudaError_t e = use_warp_mma_kernel() ? kimi::launch_decode_mma(a, s) : kimi::launch_decode_tc(a, s);
   if (e != cudaSuccess || splits == 1) return cuda_status(e);
 
   kimi::ReduceArgs r;

@@ -61,6 +61,7 @@ struct DecodeArgs {
   int64_t o_stride_h;
   float* partial_o;    // [batch, splits, heads, 512]
   float* partial_lse;  // [batch, splits, heads]
+  int* status;         // optional device word: bits set when a bounded wait gave up
   int batch;
   int num_heads;
   int num_splits;
@@ -81,6 +82,7 @@ struct ReduceArgs {
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeArgs& a, cudaStream_t stream);
+cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_reduce(const ReduceArgs& a, cudaStream_t stream);
 
 }  // namespace kimi

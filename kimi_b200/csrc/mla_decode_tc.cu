@@ -6,36 +6,43 @@
 // with the contract of `reference_mla_decode` (tests/test_triton_mla_decode.py:12-62):
 //   S = q_nope . k_nope + q_pe . k_pe,  P = softmax(S * sm_scale),  O = P . k_nope.
 //
-// Layout of one CTA (a sequence, a range of its pages, up to 64 heads):
+// One CTA = a sequence, a range of its pages, up to 64 heads.
 //   * The cache is consumed in tiles of 128 tokens (two pages).  Tokens sit on
 //     the MMA's M dimension (M = 128) and heads on N ("swap AB"), so 64 heads
 //     fill a full-rate tcgen05 MMA.
 //   * Each latent element is dequantised ONCE per tile into an 8-bit tile V''
 //     in shared memory: e2m1 -> f16 (cvt.rn.f16x2.e2m1x2), times the e8m0
-//     scale relative to a per-split reference 2^sigma (one f16x2 multiply),
-//     then the high byte of the f16, which is the e5m2 encoding of the same
-//     value.  e2m1 * 2^k has one mantissa bit, so this is exact over e5m2's
-//     29-binade range.  V'' is stored in no-swizzle core matrices
-//     (8 tokens x 16 latent bytes) and read by the tensor core twice: K-major
-//     as the A operand of S^T = V'' . Q''^T, and MN-major as the A operand of
-//     O^T = V''^T . P''^T.
+//     scale relative to a reference 2^sigma (one f16x2 multiply), then the
+//     high byte of the f16, which is the e5m2 encoding of the same value
+//     (e2m1 * 2^k has one mantissa bit, so it is exact while the exponent is
+//     in e5m2's range; sigma follows the tile maxima, see below).  V'' is
+//     stored in 128B-swizzled atoms (8 tokens x 128 latent bytes) and read by
+//     the tensor core twice: K-major as the A operand of S^T = V'' . Q''^T and
+//     MN-major as the A operand of O^T = V''^T . P''^T.
 //   * q_nope is split into two e4m3 terms with a per-head power-of-two scale
-//     a_h (q/a_h = hi + lo), stacked as one N = 128 B operand, which keeps
-//     bf16-level accuracy for QK^T at fp8 tensor rate.  q_pe . k_pe runs as a
-//     bf16 MMA into its own accumulator.
-//   * P'' = exp2(x - R_h) as two e4m3 terms (hi + residual lo, two PV MMAs
-//     into the same accumulator; one e4m3 term alone costs ~2% relative error
-//     on short contexts), with R_h a per-head offset kept within
-//     [max - 8.5, max - 6] of the running max (raised lazily, rescaling O and
-//     the softmax sums when a score exceeds it).  The O accumulator therefore
-//     holds sum_t exp2(x - R_h) V 2^-sigma; the epilogue multiplies by 2^sigma
-//     and divides by l_h = sum_t exp2(x - R_h).
-//   * TMEM (512 columns): S_hi|S_lo [0,128), S_pe [128,192), O^T [256,512)
-//     as four 128-row latent chunks of 64 head columns.
+//     a_h (q / a_h = hi + lo), stacked as one N = 128 B operand: bf16-level
+//     accuracy for QK^T at fp8 tensor rate.  q_pe . k_pe is a bf16 MMA whose
+//     A operand (k_pe) sits in TMEM.
+//   * P'' = exp2(x - R_h) is likewise two e4m3 terms (hi + residual), two PV
+//     MMAs into the same accumulator (one e4m3 term alone costs ~2% relative
+//     error on short contexts).  R_h is a per-head offset kept within
+//     [max - 8.5, max - 4] of the running max, raised lazily.
+//   * The O accumulator holds sum_t exp2(x - R_h) V 2^-sigma.  When a tile
+//     raises R_h, or needs a different sigma (its largest scale more than 13
+//     binades above, or 4 below, the reference), O and the softmax sums are
+//     rescaled in TMEM before that tile's PV.
+//   * TMEM (512 columns): S_hi|S_lo [0,128), S_pe [128,192),
+//     k_pe double buffer [192,256), O^T [256,512) as four 128-row latent
+//     chunks of 64 head columns.
 //
-// Threads: warps 0-7 dequantise and run the softmax; warp 8 owns TMEM and
-// issues the MMAs.  Every mbarrier wait is bounded; on timeout the CTA sets
-// an error bit in the status word and all threads leave at the same barrier.
+// Pipeline: warps 0-7 alternate the softmax of tile j (S(j)) and the dequant
+// of tile j+1 (D(j+1)) into the other V'' buffer; warp 8 owns TMEM and issues
+// QK(j+1) and PV(j) as soon as their inputs are ready, so the tensor core
+// overlaps the CUDA-core work.  Every mbarrier wait is bounded; on timeout
+// the CTA records the failure and all threads still meet at the same final
+// barrier.
+#include <cstddef>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math_constants.h>
@@ -52,38 +59,46 @@ constexpr int kNH = 64;             // heads per CTA (N of the MMAs)
 constexpr int kCompute = 256;       // dequant + softmax threads
 constexpr int kThreadsTC = kCompute + 32;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColSpe = 128, kColO = 256;
-constexpr uint32_t kPollLimit = 4u << 20;
+constexpr uint32_t kColS = 0, kColSpe = 128, kColKpe = 192, kColO = 256;
+constexpr uint32_t kPollLimit = 1u << 22;
 
 // Shared memory (bytes).  Core matrix (r, c) of an operand lives at
 // r * row_stride + c * 128, 16 bytes per row inside the core.
-constexpr int kOffV = 0;            // V'' e5m2, cores (token group 0..15, latent byte group 0..31): 64 KB
-constexpr int kVRow = 32 * 128;     // 4096 B per 8-token group
-constexpr int kOffQ = 65536;        // Q'' e4m3 hi rows 0..63, lo rows 64..127: 64 KB
-constexpr int kQRow = 32 * 128;
-constexpr int kOffQpe = 131072;     // q_pe bf16, cores (head group 0..7, byte group 0..7): 8 KB
-constexpr int kOffKpe = 139264;     // k_pe bf16, cores (token group 0..15, byte group 0..7): 16 KB
+// V'' (e5m2) and Q'' (e4m3) use 128B-swizzled atoms of 8 rows x 128 bytes:
+// atom (row group rg, latent column dcol) at dcol * 16 KB + rg * 1 KB, so the
+// same V'' bytes serve as a K-major (tokens x latent) and an MN-major
+// (latent x tokens) operand.
+constexpr int kVBytes = 65536;      // V'' tile: 16 token groups x 4 latent columns
+constexpr int kVCol = 16384;        // one 128-byte latent column of 16 atoms
+constexpr int kOffV = 0;            // two V'' buffers
+constexpr int kOffQ = 2 * kVBytes;  // Q'' e4m3 hi rows 0..63, lo rows 64..127 (same atom layout): 64 KB
+constexpr int kOffQpe = kOffQ + 65536;  // q_pe bf16, cores (head group 0..7, byte group 0..7): 8 KB
 constexpr int kPeRow = 8 * 128;
-constexpr int kOffP = 155648;       // P'' hi e4m3, MN-major cores (token group 0..15, head byte group 0..3): 8 KB
-constexpr int kOffPlo = 163840;     // P'' lo (residual), same layout: 8 KB
+constexpr int kOffP = kOffQpe + 8192;   // P'' hi e4m3, MN-major cores (token group 0..15, head byte group 0..3)
+constexpr int kOffPlo = kOffP + 8192;   // P'' lo (residual), same layout
 constexpr int kPRow = 4 * 128;
-constexpr int kOffMisc = 172032;
+constexpr int kOffMisc = kOffPlo + 8192;
 
 struct Misc {
-  uint64_t bar_s;
-  uint64_t bar_o;
+  uint64_t mb_s;      // QK(j) complete (tcgen05.commit)
+  uint64_t mb_o;      // PV(j) complete (tcgen05.commit)
+  uint64_t mb_vfull;  // V''(j) and k_pe(j) written (8 warp arrivals)
+  uint64_t mb_sfree;  // S(j) read out of TMEM (8 warp arrivals)
+  uint64_t mb_pfull;  // P''(j) written, O rescaled (8 warp arrivals)
   uint32_t tmem_base;
   int abort_flag;
-  int rescale_flag;
-  int sigma;              // latent reference exponent: V'' = V * 2^-sigma
-  int tile_smax[2];       // max e8m0 byte of the current tile (double-buffered reset)
-  float a[kNH];           // per-head q_nope scale (power of two)
-  float coef[kNH];        // 2^sigma * a_h * sm_scale * log2(e)
-  float R[kNH];           // per-head exp2 offset (log2 units)
-  float alpha[kNH];       // rescale factors of a rescale event
-  float red[4][kNH];      // cross-warp reduction scratch
+  int tile_smax[2];   // max e8m0 byte of the tile being dequantised (reset by parity)
+  alignas(16) float ac[kNH];  // a_h * sm_scale * log2(e)   (read as float4)
+  alignas(16) float R[kNH];   // per-head exp2 offset, log2 units (read as float4)
+  float alpha[kNH];   // O rescale factors of the current event
+  float beta[kNH];    // softmax-sum rescale factors of the current event
+  float red[4][kNH];  // cross-warp reduction scratch
 };
 constexpr int kSmemTC = kOffMisc + static_cast<int>(sizeof(Misc));
+static_assert(kSmemTC <= 232448, "shared memory budget");
+static_assert(kOffMisc % 16 == 0 && offsetof(Misc, ac) % 16 == 0 && offsetof(Misc, R) % 16 == 0,
+              "per-head arrays are read with 16-byte vector loads");
+static_assert(offsetof(Misc, mb_s) % 8 == 0 && offsetof(Misc, mb_pfull) % 8 == 0, "mbarriers are 8-byte aligned");
 
 __device__ __forceinline__ uint8_t* smem_base() {
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
@@ -94,6 +109,36 @@ __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
+// Barrier over the compute threads that also ORs a predicate across them.
+__device__ __forceinline__ bool compute_bar_or(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 4, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(out)
+      : "r"(pred ? 1u : 0u)
+      : "memory");
+  return out != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(mbar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t* mbar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(mbar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
@@ -102,101 +147,143 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return v;
 }
 
-// Four e2m1 pairs (one u32 of packed nibbles) -> four f16x2 (exact).
-__device__ __forceinline__ void cvt4_e2m1(uint32_t w, uint32_t (&o)[4]) {
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}\n"
-      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
-      : "r"(w));
+__device__ __forceinline__ uint4 ldg_cached(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
-  return d;
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// f16 2^k (k in [-24, 15]) replicated in both halves; 0 below.
-__device__ __forceinline__ uint32_t f16x2_pow2(int k) {
-  uint32_t h;
-  if (k >= -14)
-    h = static_cast<uint32_t>(k + 15) << 10;
-  else if (k >= -24)
-    h = 1u << (k + 24);
-  else
-    h = 0u;
-  return h | (h << 16);
-}
-
-// Sixteen packed nibble bytes (32 elements of one e8m0 group) times the f16
-// multiplier -> 32 e5m2 bytes (two 16-byte rows of V'').
-__device__ __forceinline__ void group_to_e5m2(const uint4& nib, uint32_t mult, uint4& out0, uint4& out1) {
-  const uint32_t w[4] = {nib.x, nib.y, nib.z, nib.w};
-  uint32_t r[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t f[4];
-    cvt4_e2m1(w[i], f);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) f[j] = hmul2_u32(f[j], mult);
-    r[2 * i] = __byte_perm(f[0], f[1], 0x7531);
-    r[2 * i + 1] = __byte_perm(f[2], f[3], 0x7531);
+// e2m1 -> e5m2 without conversion instructions.  For an e2m1 magnitude code
+// c = (e << 1) | m (c >= 2 normal: 2^(e-1) (1 + m/2); c = 1: 0.5), the e5m2
+// byte of value * 2^k is (0x38 + 4k) + 2c for c >= 2, 0x38 + 4k for c = 1 and
+// 0 for c = 0.  A group of 32 elements shares k, so the eight magnitude bytes
+// form a two-register PRMT table built once per group; the e2m1 sign (bit 3)
+// becomes the e5m2 sign (bit 7).  Exact for k in [-13, 13]; below -14 the
+// group is flushed to zero (it is then below 2^-14 of the reference).
+__device__ __forceinline__ void e5m2_tables(int k, uint32_t& lut_lo, uint32_t& lut_hi) {
+  if (k < -14) {
+    lut_lo = lut_hi = 0u;
+    return;
   }
-  out0 = make_uint4(r[0], r[1], r[2], r[3]);
-  out1 = make_uint4(r[4], r[5], r[6], r[7]);
+  lut_lo = 0x3E3C3800u + 0x04040400u * static_cast<uint32_t>(k);
+  lut_hi = 0x46444240u + 0x04040404u * static_cast<uint32_t>(k);
 }
 
-// Raw data of one tile held by one thread: for its token, 16-byte chunk
-// j = 2k + e of the nibbles (k = 0..7) and of the RoPE bytes (k = 0..3),
-// plus the token's 16 scale bytes.
-struct TileRegs {
-  uint4 nib[8];
-  uint4 pe[4];
-  uint4 sc;
-  int valid;
-};
+// Eight e2m1 values (one u32 of packed nibbles, element 2j in the low nibble
+// of byte j) -> eight e5m2 bytes in element order.
+__device__ __forceinline__ void e2m1x8_to_e5m2(uint32_t w, uint32_t lut_lo, uint32_t lut_hi, uint32_t& o0,
+                                               uint32_t& o1) {
+  const uint32_t m0 = __byte_perm(lut_lo, lut_hi, w & 0x7777u);          // magnitudes of elements 0..3
+  const uint32_t m1 = __byte_perm(lut_lo, lut_hi, (w >> 16) & 0x7777u);  // elements 4..7
+  const uint32_t y0 = __byte_perm(w, 0u, 0x1100);                        // bytes b0 b0 b1 b1
+  const uint32_t y1 = __byte_perm(w, 0u, 0x3322);                        // bytes b2 b2 b3 b3
+  // sign of element 2j sits in bit 3 of byte j, of element 2j+1 in bit 7
+  o0 = m0 | ((y0 << 4) & 0x00800080u) | (y0 & 0x80008000u);
+  o1 = m1 | ((y1 << 4) & 0x00800080u) | (y1 & 0x80008000u);
+}
+
+// Sixteen packed nibble bytes (32 elements of one e8m0 group) with shift k ->
+// 32 e5m2 bytes (two 16-byte rows of V'').
+__device__ __forceinline__ void group_to_e5m2(const uint4& nib, int k, uint4& out0, uint4& out1) {
+  uint32_t lo, hi;
+  e5m2_tables(k, lo, hi);
+  e2m1x8_to_e5m2(nib.x, lo, hi, out0.x, out0.y);
+  e2m1x8_to_e5m2(nib.y, lo, hi, out0.z, out0.w);
+  e2m1x8_to_e5m2(nib.z, lo, hi, out1.x, out1.y);
+  e2m1x8_to_e5m2(nib.w, lo, hi, out1.z, out1.w);
+}
+
+// p (two floats) -> e4m3 hi and e4m3 residual, through f16 (exact residual).
+__device__ __forceinline__ void split_e4m3x2(float p0, float p1, uint16_t& hi, uint16_t& lo) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %2, %1;\n" : "=r"(h) : "f"(p0), "f"(p1));
+  uint16_t h8;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;\n" : "=h"(h8) : "r"(h));
+  uint32_t back;
+  asm("{\n\t.reg .b16 t;\n\tmov.b16 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}\n" : "=r"(back) : "h"(h8));
+  uint32_t res;
+  asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(res) : "r"(h), "r"(back));
+  uint16_t l8;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;\n" : "=h"(l8) : "r"(res));
+  hi = h8;
+  lo = l8;
+}
 
 struct WorkItem {
   int b, split, head_base, heads_here;
   int page_lo, n_pages, n_tok, p_begin, p_end;
 };
 
-__device__ __forceinline__ int tile_page(const DecodeArgs& a, const WorkItem& w, int tile, int slot) {
-  const int p = w.p_begin + 2 * tile + slot;
-  if (p >= w.p_end) return -1;
-  const int page = a.kv_indices[w.page_lo + p];
-  return (page >= 0 && page < a.num_pages) ? page : -1;
+// Number of this split's tokens in tile j (arithmetic only).
+__device__ __forceinline__ int tile_valid(const WorkItem& w, int tile) {
+  const int p0 = w.p_begin + 2 * tile;
+  return max(0, min(min(kPageSize * 2, w.n_tok - p0 * kPageSize), (w.p_end - p0) * kPageSize));
 }
 
-__device__ __forceinline__ void load_tile(const DecodeArgs& a, const WorkItem& w, int tile, int t, int e,
-                                          TileRegs& r) {
-  const int page = tile_page(a, w, tile, t >> 6);
-  const int seq_tok = (w.p_begin + 2 * tile) * kPageSize + t;
-  r.valid = page >= 0 && seq_tok < w.n_tok;
-  if (r.valid) {
-    const uint8_t* row = a.kv_buffer + static_cast<int64_t>(page) * kPageBytes + (t & 63) * kTokenBytes;
+// Raw data of one tile held by one thread.  Latent nibbles follow the loader
+// mapping: warp w covers tokens 16w..16w+15; in load i (0..7) lanes 0-15 read
+// the sixteen 16-byte chunks (= e8m0 groups) of token 16w + 2i and lanes 16-31
+// those of token 16w + 2i + 1, so every load instruction reads four whole
+// 128-byte lines.  A thread thus holds group g = lane % 16 of eight tokens,
+// with the matching scale bytes.  RoPE follows the TMEM mapping (token st,
+// bytes [64 hf, 64 hf + 64)).
+struct TileRegs {
+  uint4 nib[8];
+  uint32_t sb[8];         // scale byte of group g for each of the eight tokens
+  uint4 pe[4];
+  int nvalid;
+  int page_next[2];       // page ids of the tile loaded next (fetched one tile ahead)
+};
+
+__device__ __forceinline__ void fetch_pages(const DecodeArgs& a, const WorkItem& w, int tile, int (&pg)[2]) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) r.nib[k] = ldg_stream(row + 16 * (2 * k + e));
-#pragma unroll
-    for (int k = 0; k < 4; ++k) r.pe[k] = ldg_stream(row + kNibbleBytes + 16 * (2 * k + e));
-    r.sc = ldg_stream(a.kv_scales + static_cast<int64_t>(page) * kPageScaleBytes + (t & 63) * kScaleBytes);
+  for (int slot = 0; slot < 2; ++slot) {
+    const int p = w.p_begin + 2 * tile + slot;
+    pg[slot] = p < w.p_end ? __ldg(a.kv_indices + w.page_lo + p) : -1;
   }
 }
 
-__device__ __forceinline__ uint32_t max_byte(const uint4& v) {
-  uint32_t m = __vmaxu4(__vmaxu4(v.x, v.y), __vmaxu4(v.z, v.w));
-  m = __vmaxu4(m, m >> 16);
-  m = __vmaxu4(m, m >> 8);
-  return m & 0xFFu;
-}
-
-__device__ __forceinline__ uint32_t scale_byte(const uint4& v, int g) {
-  const uint32_t w = g < 4 ? v.x : (g < 8 ? v.y : (g < 12 ? v.z : v.w));
-  return (w >> (8 * (g & 3))) & 0xFFu;
+__device__ __forceinline__ void load_tile(const DecodeArgs& a, const WorkItem& w, int tile, int warp, int lane,
+                                          int st, int hf, TileRegs& r) {
+  const int nvalid = tile_valid(w, tile);
+  r.nvalid = nvalid;
+  const int pg[2] = {r.page_next[0], r.page_next[1]};
+  const int e = lane >> 4, g = lane & 15;
+  const int slot = warp >> 2;  // tokens 16w..16w+15 lie in one page
+  const int page = (pg[slot] >= 0 && pg[slot] < a.num_pages) ? pg[slot] : -1;
+  const uint8_t* pbase = a.kv_buffer + static_cast<int64_t>(page < 0 ? 0 : page) * kPageBytes;
+  const uint8_t* sbase = a.kv_scales + static_cast<int64_t>(page < 0 ? 0 : page) * kPageScaleBytes;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int tk = 16 * warp + 2 * i + e;
+    if (page >= 0 && tk < nvalid) {
+      r.nib[i] = ldg_stream(pbase + (tk & 63) * kTokenBytes + 16 * g);
+      r.sb[i] = __ldg(sbase + (tk & 63) * kScaleBytes + g);
+    } else {
+      r.nib[i] = make_uint4(0, 0, 0, 0);
+      r.sb[i] = 0u;
+    }
+  }
+  const int pslot = st >> 6;
+  const int ppage = (pg[pslot] >= 0 && pg[pslot] < a.num_pages && st < nvalid) ? pg[pslot] : -1;
+  if (ppage >= 0) {
+    const uint8_t* row = a.kv_buffer + static_cast<int64_t>(ppage) * kPageBytes + (st & 63) * kTokenBytes +
+                         kNibbleBytes + 64 * hf;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r.pe[k] = ldg_cached(row + 16 * k);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r.pe[k] = make_uint4(0, 0, 0, 0);
+  }
+  fetch_pages(a, w, tile + 1, r.page_next);
 }
 
 // Transpose-reduce (max or sum) of 32 per-lane values over the warp: lane j
@@ -221,7 +308,144 @@ __device__ __forceinline__ void record_status(const DecodeArgs& a, int bits) {
   if (a.status) atomicOr(a.status, bits);
 }
 
-__global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs a) {
+__device__ __forceinline__ bool wait_or_abort(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit) {
+  if (mbar_wait_bounded(mb, parity, kPollLimit)) return true;
+  atomicExch(&ms.abort_flag, 1);
+  record_status(a, bit);
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// MMA issuer (warp 8, lane 0 issues)
+// ---------------------------------------------------------------------------
+__device__ void mma_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int lane, const DecodeArgs& a) {
+  const uint32_t id_qk = instr_desc(kFmtE5M2, kFmtE4M3, false, false, 128, 128);
+  const uint32_t id_pe = instr_desc(kFmtBF16, kFmtBF16, false, false, 128, 64);
+  const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, 64);
+  const uint32_t sQ = smem_addr(sm + kOffQ), sQpe = smem_addr(sm + kOffQpe);
+  const uint32_t sP = smem_addr(sm + kOffP), sPlo = smem_addr(sm + kOffPlo);
+  int qk_next = 0, pv_next = 0;
+  uint32_t idle = 0;
+  while (pv_next < n_tiles) {
+    bool progressed = false;
+    // QK(j) needs V''(j) written and S(j-1) read out of TMEM (single S buffer).
+    if (qk_next < n_tiles && qk_next <= pv_next + 1 && mbar_test(&ms.mb_vfull, qk_next & 1) &&
+        (qk_next == 0 || mbar_test(&ms.mb_sfree, (qk_next - 1) & 1))) {
+      fence_after_sync();
+      if (lane == 0) {
+        const uint32_t sV = smem_addr(sm + kOffV + (qk_next & 1) * kVBytes);
+        // The 16 latent MMAs chain on one accumulator; the 4 RoPE MMAs (own
+        // accumulator) are interleaved so they fill the chain's latency.
+        const uint32_t kpe = tmem + kColKpe + 32 * (qk_next & 1);
+#pragma unroll 1
+        for (int k = 0; k < 16; ++k) {
+          const uint32_t koff = (k >> 2) * kVCol + (k & 3) * 32;
+          mma_f8f6f4_ss(tmem + kColS, smem_desc(sV + koff, 16, 1024, kSwizzle128B),
+                        smem_desc(sQ + koff, 16, 1024, kSwizzle128B), id_qk, k > 0);
+          if (k < 4)
+            mma_f16_ts(tmem + kColSpe, kpe + 8 * k, smem_desc(sQpe + k * 256, 128, kPeRow), id_pe, k > 0);
+        }
+        mma_commit(&ms.mb_s);
+      }
+      __syncwarp();
+      ++qk_next;
+      progressed = true;
+    }
+    // PV(j) needs P''(j) (written after PV(j-1) completed and O was rescaled).
+    if (pv_next < qk_next && mbar_test(&ms.mb_pfull, pv_next & 1)) {
+      fence_after_sync();
+      if (lane == 0) {
+        const uint32_t sV = smem_addr(sm + kOffV + (pv_next & 1) * kVBytes);
+        // Consecutive MMAs go to different latent chunks (independent
+        // accumulators), so they pipeline instead of chaining.
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t phi = smem_desc(sP + k * 4 * kPRow, kPRow, 128);
+          const uint64_t plo = smem_desc(sPlo + k * 4 * kPRow, kPRow, 128);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B),
+                          phi, id_pv, (pv_next > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B),
+                          plo, id_pv, 1u);
+        }
+        mma_commit(&ms.mb_o);
+      }
+      __syncwarp();
+      ++pv_next;
+      progressed = true;
+    }
+    if (progressed) {
+      idle = 0;
+    } else if (++idle > kPollLimit || ms.abort_flag) {
+      atomicExch(&ms.abort_flag, 1);
+      record_status(a, 8);
+      break;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dequant of one tile into a V'' buffer and a k_pe TMEM buffer
+// ---------------------------------------------------------------------------
+// Returns the reference exponent sigma chosen for the tile (identical in every thread).
+__device__ __forceinline__ int dequant_tile(uint8_t* sm, Misc& ms, uint32_t tmem, uint32_t lane_base, int tile,
+                                            int prev_sigma, const TileRegs& r, int warp, int lane, int hf, int tid) {
+  const int buf = tile & 1;
+  // tile maximum of the e8m0 bytes (invalid tokens carry 0) -> reference exponent
+  uint32_t my_max = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) my_max = max(my_max, r.sb[i]);
+  my_max = __reduce_max_sync(0xffffffffu, my_max);
+  if (lane == 0) atomicMax(&ms.tile_smax[buf], static_cast<int>(my_max));
+  named_bar(4, kCompute);
+  const int smax = ms.tile_smax[buf];
+  int sigma;
+  if (tile == 0) {
+    sigma = smax - 127 - 8;  // tile max maps to <= 6 * 2^8 in V''
+  } else {
+    const int kmax = smax - 127 - prev_sigma;
+    sigma = (kmax > 13 || kmax < -4) ? smax - 127 - 8 : prev_sigma;
+  }
+  if (tid == 0) ms.tile_smax[buf ^ 1] = 0;
+
+  // group g of eight tokens -> two 16-byte chunks (latent bytes 32g .. 32g + 31) each
+  const int e = lane >> 4, g = lane & 15;
+  uint8_t* vb = sm + kOffV + buf * kVBytes + (g >> 2) * kVCol;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int tk = 16 * warp + 2 * i + e;
+    const uint32_t sbyte = r.sb[i];
+    uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
+    if (tk < r.nvalid) group_to_e5m2(r.nib[i], static_cast<int>(sbyte) - 127 - sigma, o0, o1);
+    uint8_t* atom = vb + (tk >> 3) * 1024;
+    *reinterpret_cast<uint4*>(atom + sw128_offset(tk & 7, (2 * g) & 7)) = o0;
+    *reinterpret_cast<uint4*>(atom + sw128_offset(tk & 7, (2 * g + 1) & 7)) = o1;
+  }
+  // k_pe -> TMEM columns [kColKpe + 32 buf + 16 hf, +16) of this thread's TMEM lane
+  {
+    uint32_t v[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[4 * k] = r.pe[k].x;
+      v[4 * k + 1] = r.pe[k].y;
+      v[4 * k + 2] = r.pe[k].z;
+      v[4 * k + 3] = r.pe[k].w;
+    }
+    tmem_st16(tmem + lane_base + kColKpe + 32 * buf + 16 * hf, v);
+    tmem_st_wait();
+  }
+  fence_proxy_async_smem();
+  fence_before_sync();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&ms.mb_vfull);
+  return sigma;
+}
+
+// Nine warps put three on one SM sub-partition (16K registers): at most 168 registers per thread.
+__global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __grid_constant__ DecodeArgs a) {
   uint8_t* sm = smem_base();
   Misc& ms = *reinterpret_cast<Misc*>(sm + kOffMisc);
   const int tid = threadIdx.x;
@@ -234,13 +458,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
   w.head_base = blockIdx.z * kNH;
   w.heads_here = min(kNH, a.num_heads - w.head_base);
   w.page_lo = a.kv_indptr[w.b];
-  w.n_pages = a.kv_indptr[w.b + 1] - w.page_lo;
+  w.n_pages = max(a.kv_indptr[w.b + 1] - w.page_lo, 0);
   const int last_len =
-      w.n_pages <= 0 ? 0 : min(max(a.kv_last_page_len ? a.kv_last_page_len[w.b] : kPageSize, 1), kPageSize);
-  w.n_tok = w.n_pages <= 0 ? 0 : (w.n_pages - 1) * kPageSize + last_len;
-  const int pps = 2 * ((max(w.n_pages, 0) + 2 * a.num_splits - 1) / (2 * a.num_splits));
+      w.n_pages == 0 ? 0 : min(max(a.kv_last_page_len ? a.kv_last_page_len[w.b] : kPageSize, 1), kPageSize);
+  w.n_tok = w.n_pages == 0 ? 0 : (w.n_pages - 1) * kPageSize + last_len;
+  const int pps = 2 * ((w.n_pages + 2 * a.num_splits - 1) / (2 * a.num_splits));
   w.p_begin = w.split * pps;
-  w.p_end = min(w.p_begin + pps, max(w.n_pages, 0));
+  w.p_end = min(w.p_begin + pps, w.n_pages);
   const bool direct = a.num_splits == 1;
 
   if (w.p_begin >= w.p_end) {
@@ -262,11 +486,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
   if (warp == 8) {
     tmem_alloc(&ms.tmem_base, kTmemCols);
     if (lane == 0) {
-      mbar_init(&ms.bar_s, 1);
-      mbar_init(&ms.bar_o, 1);
+      mbar_init(&ms.mb_s, 1);
+      mbar_init(&ms.mb_o, 1);
+      mbar_init(&ms.mb_vfull, 8);
+      mbar_init(&ms.mb_sfree, 8);
+      mbar_init(&ms.mb_pfull, 8);
       fence_mbar_init();
       ms.abort_flag = 0;
-      ms.rescale_flag = 0;
       ms.tile_smax[0] = 0;
       ms.tile_smax[1] = 0;
     }
@@ -292,7 +518,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
     if (amax == 0.f || ex < -126) ex = 0;
     const float a_h = __uint_as_float(static_cast<uint32_t>(ex + 127) << 23);
     const float inv_a = __uint_as_float(static_cast<uint32_t>(127 - ex) << 23);
-    if (part == 0) ms.a[h] = a_h;
+    if (part == 0) {
+      ms.ac[h] = a_h * c_log2;
+      ms.R[h] = 0.f;
+    }
     uint8_t* qb = sm + kOffQ;
 #pragma unroll
     for (int k = 0; k < 16; k += 2) {
@@ -301,28 +530,26 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
       const uint32_t ws[8] = {qv[k].x, qv[k].y, qv[k].z, qv[k].w, qv[k + 1].x, qv[k + 1].y, qv[k + 1].z, qv[k + 1].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float x[4];
-        x[0] = __uint_as_float(ws[2 * j] << 16) * inv_a;
-        x[1] = __uint_as_float(ws[2 * j] & 0xFFFF0000u) * inv_a;
-        x[2] = __uint_as_float(ws[2 * j + 1] << 16) * inv_a;
-        x[3] = __uint_as_float(ws[2 * j + 1] & 0xFFFF0000u) * inv_a;
-        const uint16_t h01 = cvt_f32x2_e4m3x2(x[0], x[1]);
-        const uint16_t h23 = cvt_f32x2_e4m3x2(x[2], x[3]);
-        // residuals against the e4m3 values (e4m3 -> float is exact)
-        const float2 g01 = e4m3x2_to_float2(h01);
+        const float x0 = __uint_as_float(ws[2 * j] << 16) * inv_a;
+        const float x1 = __uint_as_float(ws[2 * j] & 0xFFFF0000u) * inv_a;
+        const float x2 = __uint_as_float(ws[2 * j + 1] << 16) * inv_a;
+        const float x3 = __uint_as_float(ws[2 * j + 1] & 0xFFFF0000u) * inv_a;
+        const uint16_t h01 = cvt_f32x2_e4m3x2(x0, x1);
+        const uint16_t h23 = cvt_f32x2_e4m3x2(x2, x3);
+        const float2 g01 = e4m3x2_to_float2(h01);  // exact
         const float2 g23 = e4m3x2_to_float2(h23);
-        const uint16_t l01 = cvt_f32x2_e4m3x2(x[0] - g01.x, x[1] - g01.y);
-        const uint16_t l23 = cvt_f32x2_e4m3x2(x[2] - g23.x, x[3] - g23.y);
+        const uint16_t l01 = cvt_f32x2_e4m3x2(x0 - g01.x, x1 - g01.y);
+        const uint16_t l23 = cvt_f32x2_e4m3x2(x2 - g23.x, x3 - g23.y);
         hi_w[j] = static_cast<uint32_t>(h01) | (static_cast<uint32_t>(h23) << 16);
         lo_w[j] = static_cast<uint32_t>(l01) | (static_cast<uint32_t>(l23) << 16);
       }
-      const int dc = 8 * part + k / 2;  // 16-byte latent group of this row (0..31)
-      *reinterpret_cast<uint4*>(qb + (h >> 3) * kQRow + dc * 128 + (h & 7) * 16) =
+      const int dc = 8 * part + k / 2;  // 16-byte latent chunk of this row (0..31)
+      uint8_t* col = qb + (dc >> 3) * kVCol;
+      *reinterpret_cast<uint4*>(col + (h >> 3) * 1024 + sw128_offset(h & 7, dc & 7)) =
           make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
-      *reinterpret_cast<uint4*>(qb + (8 + (h >> 3)) * kQRow + dc * 128 + (h & 7) * 16) =
+      *reinterpret_cast<uint4*>(col + (8 + (h >> 3)) * 1024 + sw128_offset(h & 7, dc & 7)) =
           make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
     }
-    // q_pe: 16 bf16 = two 16-byte core rows
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + kLatent + 16 * part + 8 * k) : make_uint4(0, 0, 0, 0);
@@ -336,60 +563,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
   const uint32_t tmem = ms.tmem_base;
 
   if (warp == 8) {
-    // ---------------- MMA issuer ----------------
-    const uint32_t id_qk = instr_desc(kFmtE5M2, kFmtE4M3, false, false, 128, 128);
-    const uint32_t id_pe = instr_desc(kFmtBF16, kFmtBF16, false, false, 128, 64);
-    const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, 64);
-    const uint32_t sV = smem_addr(sm + kOffV), sQ = smem_addr(sm + kOffQ);
-    const uint32_t sQpe = smem_addr(sm + kOffQpe), sKpe = smem_addr(sm + kOffKpe), sP = smem_addr(sm + kOffP);
-    const uint32_t sPlo = smem_addr(sm + kOffPlo);
-    for (int tile = 0; tile < n_tiles; ++tile) {
-      named_bar(1, kThreadsTC);  // tile ready
-      if (ms.abort_flag) break;
-      fence_after_sync();
-      if (lane == 0) {
-#pragma unroll 1
-        for (int k = 0; k < 16; ++k)
-          mma_f8f6f4_ss(tmem + kColS, smem_desc(sV + k * 256, 128, kVRow), smem_desc(sQ + k * 256, 128, kQRow), id_qk,
-                        k > 0);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_f16_ss(tmem + kColSpe, smem_desc(sKpe + k * 256, 128, kPeRow), smem_desc(sQpe + k * 256, 128, kPeRow),
-                     id_pe, k > 0);
-        mma_commit(&ms.bar_s);
-      }
-      __syncwarp();
-      named_bar(2, kThreadsTC);  // P ready
-      if (ms.abort_flag) break;
-      fence_after_sync();
-      if (lane == 0) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t va = smem_desc(sV + k * 4 * kVRow + c * 8 * 128, kVRow, 128);
-            mma_f8f6f4_ss(tmem + kColO + 64 * c, va, smem_desc(sP + k * 4 * kPRow, kPRow, 128), id_pv,
-                          (tile > 0 || k > 0) ? 1u : 0u);
-            mma_f8f6f4_ss(tmem + kColO + 64 * c, va, smem_desc(sPlo + k * 4 * kPRow, kPRow, 128), id_pv, 1u);
-          }
-        mma_commit(&ms.bar_o);
-      }
-      __syncwarp();
-    }
+    mma_issuer(sm, ms, tmem, n_tiles, lane, a);
+    fence_before_sync();
     named_bar(3, kThreadsTC);  // epilogue done
     fence_after_sync();
     tmem_dealloc(tmem, kTmemCols);
     return;
   }
 
-  // ---------------- compute warps: dequant + softmax ----------------
-  // Loader mapping: warp covers tokens 16*warp..+16; lanes l and l+16 share a token.
-  const int lt = 16 * warp + (lane & 15);
-  const int le = lane >> 4;
-  // TMEM mapping: quadrant q = warp & 3 owns lanes / tokens 32q..32q+31; hf picks heads 32hf..+32.
-  const int q = warp & 3;
-  const int hf = warp >> 2;
-  const int st = 32 * q + lane;  // token of this thread in the softmax
+  // ---------------- compute warps ----------------
+  const int q = warp & 3;                  // TMEM lane quadrant
+  const int hf = warp >> 2;                // heads 32 hf .. 32 hf + 31
+  const int st = 32 * q + lane;            // softmax token
   const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
 
   float l_part[32];
@@ -397,136 +582,82 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
   for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
 
   TileRegs r;
-  load_tile(a, w, 0, lt, le, r);
-  bool aborted = false;
+  fetch_pages(a, w, 0, r.page_next);
+  load_tile(a, w, 0, warp, lane, st, hf, r);
+  // sigma of the tile in V'' buffer 0 / 1 (every compute thread holds the same values)
+  int sig_buf0 = dequant_tile(sm, ms, tmem, lane_base, 0, 0, r, warp, lane, hf, tid);
+  int sig_buf1 = sig_buf0;
+  if (n_tiles > 1) load_tile(a, w, 1, warp, lane, st, hf, r);
+  int sigma_prev = sig_buf0;
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     const uint32_t par = static_cast<uint32_t>(tile & 1);
-    // Previous PV must be done before V'', k_pe and P'' are overwritten and before O is rescaled.
-    if (tile > 0 && !mbar_wait_bounded(&ms.bar_o, par ^ 1u, kPollLimit)) {
-      atomicExch(&ms.abort_flag, 1);
-      record_status(a, 1);
-    }
+    // ---------------- S(j): softmax of tile j ----------------
+    wait_or_abort(&ms.mb_s, par, ms, a, 1);
     fence_after_sync();
-
-    // ---- tile max of the e8m0 bytes (valid tokens) ----
-    uint32_t my_max = r.valid ? max_byte(r.sc) : 0u;
-    my_max = __reduce_max_sync(0xffffffffu, my_max);
-    if (lane == 0) atomicMax(&ms.tile_smax[par], static_cast<int>(my_max));
-    named_bar(4, kCompute);
-    const int tmax = ms.tile_smax[par];
-    if (tid == 0) ms.tile_smax[par ^ 1] = 0;
-    if (tile == 0 || tmax > ms.sigma + 127 + 13) {
-      const int new_sigma = tmax - 127 - 8;  // tile max maps to <= 6 * 2^8 in V''
-      if (tile > 0) {
-        // raise sigma: O *= 2^(old - new) for every head (TMEM read-modify-write)
-        const float f = exp2f(static_cast<float>(ms.sigma - new_sigma));
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * hf + cc;
-#pragma unroll 1
-          for (int half = 0; half < 2; ++half) {
-            uint32_t v[32];
-            const uint32_t ta = tmem + lane_base + kColO + 64 * c + 32 * half;
-            tmem_ld32(ta, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * f);
-            tmem_st32(ta, v);
-          }
-        }
-        tmem_st_wait();
-      }
-      named_bar(4, kCompute);
-      if (tid < kNH) ms.coef[tid] = exp2f(static_cast<float>(new_sigma)) * ms.a[tid] * c_log2;
-      if (tid == 0) ms.sigma = new_sigma;
-      named_bar(4, kCompute);
-    }
-    const int sigma = ms.sigma;
-
-    // ---- dequant this thread's token into V'' and k_pe ----
+    float t[32];
     {
-      uint8_t* vrow = sm + kOffV + (lt >> 3) * kVRow + (lt & 7) * 16;
-      uint8_t* prow = sm + kOffKpe + (lt >> 3) * kPeRow + (lt & 7) * 16;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int g = 2 * k + le;  // e8m0 group == 16-byte nibble chunk
-        uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
-        if (r.valid) {
-          const int kexp = static_cast<int>(scale_byte(r.sc, g)) - 127 - sigma;
-          group_to_e5m2(r.nib[k], f16x2_pow2(kexp), o0, o1);
-        }
-        *reinterpret_cast<uint4*>(vrow + (2 * g) * 128) = o0;
-        *reinterpret_cast<uint4*>(vrow + (2 * g + 1) * 128) = o1;
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        *reinterpret_cast<uint4*>(prow + (2 * k + le) * 128) = r.valid ? r.pe[k] : make_uint4(0, 0, 0, 0);
-    }
-    if (tile + 1 < n_tiles) load_tile(a, w, tile + 1, lt, le, r);
-    fence_proxy_async_smem();
-    fence_before_sync();
-    named_bar(1, kThreadsTC);  // tile ready
-    if (ms.abort_flag) {
-      aborted = true;
-      break;
-    }
-
-    // ---- softmax on S^T rows (this thread: token st, heads 32hf..32hf+31) ----
-    if (!mbar_wait_bounded(&ms.bar_s, par, kPollLimit)) {
-      atomicExch(&ms.abort_flag, 1);
-      record_status(a, 2);
-    }
-    fence_after_sync();
-    float x[32];
-    {
-      uint32_t s_hi[32], s_lo[32], s_pe[32];
+      uint32_t s_hi[32], s_lo[32];
       tmem_ld32(tmem + lane_base + kColS + 32 * hf, s_hi);
       tmem_ld32(tmem + lane_base + kColS + 64 + 32 * hf, s_lo);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(s_hi[j]) + __uint_as_float(s_lo[j]);
+      uint32_t s_pe[32];
       tmem_ld32(tmem + lane_base + kColSpe + 32 * hf, s_pe);
       tmem_ld_wait();
-      const int seq_tok = (w.p_begin + 2 * tile) * kPageSize + st;
-      const bool tvalid = tile_page(a, w, tile, st >> 6) >= 0 && seq_tok < w.n_tok;
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ms.mb_sfree);
+      const int sigma = par ? sig_buf1 : sig_buf0;
+      const float sig = __uint_as_float(static_cast<uint32_t>(min(max(sigma + 127, 1), 254)) << 23);
+      const bool tvalid = st < tile_valid(w, tile);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float s = __uint_as_float(s_hi[j]) + __uint_as_float(s_lo[j]);
-        x[j] = tvalid ? fmaf(s, ms.coef[32 * hf + j], __uint_as_float(s_pe[j]) * c_log2) : -CUDART_INF_F;
+      for (int j = 0; j < 32; j += 4) {
+        const float4 ac4 = *reinterpret_cast<const float4*>(&ms.ac[32 * hf + j]);
+        const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[32 * hf + j]);
+        const float acv[4] = {ac4.x, ac4.y, ac4.z, ac4.w};
+        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float base = fmaf(__uint_as_float(s_pe[j + u]), c_log2, -rv[u]);
+          t[j + u] = tvalid ? fmaf(t[j + u], acv[u] * sig, base) : -CUDART_INF_F;
+        }
       }
     }
-    fence_before_sync();
-
-    // offsets: first tile sets R = max - 6; later tiles raise R when a score exceeds R + 8.5
-    bool need = tile == 0;
-    if (!need) {
-      float ymax = -CUDART_INF_F;
+    // rescale event: first tile, a score above R + 8.5, or a new sigma
+    float tmaxv = -CUDART_INF_F;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) ymax = fmaxf(ymax, x[j] - ms.R[32 * hf + j]);
-      if (__any_sync(0xffffffffu, ymax > 8.5f) && lane == 0) ms.rescale_flag = 1;
-      named_bar(4, kCompute);
-      need = ms.rescale_flag != 0;
-      named_bar(4, kCompute);
-      if (tid == 0) ms.rescale_flag = 0;
+    for (int j = 0; j < 32; ++j) tmaxv = fmaxf(tmaxv, t[j]);
+    const int sigma_cur = par ? sig_buf1 : sig_buf0;
+    const bool need = compute_bar_or(tile == 0 || tmaxv > 8.5f || sigma_cur != sigma_prev);
+    if (tile > 0) {
+      // PV(j-1) must be complete before O is rescaled or P'' is overwritten
+      wait_or_abort(&ms.mb_o, par ^ 1u, ms, a, 2);
+      fence_after_sync();
     }
     if (need) {
       float v[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = x[j];
-      const float m = warp_transpose_reduce<true>(v, lane);  // head 32hf + lane, over this warp's tokens
-      ms.red[q][32 * hf + lane] = m;
+      for (int j = 0; j < 32; ++j) v[j] = t[j];
+      ms.red[q][32 * hf + lane] = warp_transpose_reduce<true>(v, lane);  // tile max of x - R_old
       named_bar(4, kCompute);
       if (tid < kNH) {
-        const float tmx = fmaxf(fmaxf(ms.red[0][tid], ms.red[1][tid]), fmaxf(ms.red[2][tid], ms.red[3][tid]));
-        const float r_old = tile == 0 ? -CUDART_INF_F : ms.R[tid];
-        const float r_new = fmaxf(fmaxf(r_old, tmx - 6.0f), -1e30f);
-        ms.alpha[tid] = tile == 0 ? 1.0f : exp2f(r_old - r_new);
-        ms.R[tid] = r_new;
+        const float tm = fmaxf(fmaxf(ms.red[0][tid], ms.red[1][tid]), fmaxf(ms.red[2][tid], ms.red[3][tid]));
+        // raise R so that this tile's max maps to 2^4 (only raise; the first tile sets it)
+        const float shift = tile == 0 ? tm - 4.0f : fmaxf(tm - 4.0f, 0.0f);
+        const float dshift = fmaxf(shift, -1e30f);
+        ms.R[tid] += dshift;
+        ms.beta[tid] = tile == 0 ? 1.0f : ex2(-dshift);
+        ms.alpha[tid] = tile == 0 ? 1.0f : ex2(-dshift + static_cast<float>(sigma_prev - sigma_cur));
+        ms.red[0][tid] = dshift;  // reused below as the per-head shift of t
       }
       named_bar(4, kCompute);
-      if (tile > 0) {
-        // rescale the running sums and O^T columns of every head
 #pragma unroll
-        for (int j = 0; j < 32; ++j) l_part[j] *= ms.alpha[32 * hf + j];
-        fence_after_sync();
+      for (int j = 0; j < 32; ++j) t[j] -= ms.red[0][32 * hf + j];
+      if (tile > 0) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) l_part[j] *= ms.beta[32 * hf + j];
 #pragma unroll 1
         for (int cc = 0; cc < 2; ++cc) {
           const int c = 2 * hf + cc;
@@ -537,34 +668,32 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
             tmem_ld32(ta, vv);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              vv[j] = __float_as_uint(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
+            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
             tmem_st32(ta, vv);
           }
         }
         tmem_st_wait();
-        fence_before_sync();
       }
     }
+    sigma_prev = sigma_cur;
 
-    // ---- P'' = exp2(x - R) as e4m3 hi + e4m3 residual, into the MN-major B operands ----
+    // ---- P'' = exp2(t) as e4m3 hi + residual, into the MN-major B operands ----
     {
       uint32_t pw[8], pl[8];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
-        const float p0 = exp2f(x[j] - ms.R[32 * hf + j]);
-        const float p1 = exp2f(x[j + 1] - ms.R[32 * hf + j + 1]);
+        const float p0 = ex2(t[j]);
+        const float p1 = ex2(t[j + 1]);
         l_part[j] += p0;
         l_part[j + 1] += p1;
-        const uint16_t h01 = cvt_f32x2_e4m3x2(p0, p1);
-        const float2 hf01 = e4m3x2_to_float2(h01);
-        const uint16_t l01 = cvt_f32x2_e4m3x2(p0 - hf01.x, p1 - hf01.y);
+        uint16_t h8, l8;
+        split_e4m3x2(p0, p1, h8, l8);
         if ((j & 2) == 0) {
-          pw[j / 4] = h01;
-          pl[j / 4] = l01;
+          pw[j / 4] = h8;
+          pl[j / 4] = l8;
         } else {
-          pw[j / 4] |= static_cast<uint32_t>(h01) << 16;
-          pl[j / 4] |= static_cast<uint32_t>(l01) << 16;
+          pw[j / 4] |= static_cast<uint32_t>(h8) << 16;
+          pl[j / 4] |= static_cast<uint32_t>(l8) << 16;
         }
       }
       const int prow = (st >> 3) * kPRow + (st & 7) * 16;
@@ -575,28 +704,31 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
     }
     fence_proxy_async_smem();
     fence_before_sync();
-    named_bar(2, kThreadsTC);  // P ready
-    if (ms.abort_flag) {
-      aborted = true;
-      break;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms.mb_pfull);
+
+    // ---------------- D(j+1): dequant the next tile into the other buffer ----------------
+    // (V'' buffer (j+1)&1 was last read by PV(j-1), complete above; its k_pe buffer by QK(j-1).)
+    if (tile + 1 < n_tiles) {
+      const int sg = dequant_tile(sm, ms, tmem, lane_base, tile + 1, sigma_cur, r, warp, lane, hf, tid);
+      if (par)
+        sig_buf0 = sg;
+      else
+        sig_buf1 = sg;
+      if (tile + 2 < n_tiles) load_tile(a, w, tile + 2, warp, lane, st, hf, r);
     }
   }
 
   // ---------------- epilogue ----------------
-  if (!aborted && !mbar_wait_bounded(&ms.bar_o, static_cast<uint32_t>((n_tiles - 1) & 1), kPollLimit)) {
-    atomicExch(&ms.abort_flag, 1);
-    record_status(a, 4);
-  }
+  wait_or_abort(&ms.mb_o, static_cast<uint32_t>((n_tiles - 1) & 1), ms, a, 4);
   fence_after_sync();
-  // l_h: sum of this warp's tokens, then over the four quadrants
   {
     const float s = warp_transpose_reduce<false>(l_part, lane);
     ms.red[q][32 * hf + lane] = s;
   }
   named_bar(4, kCompute);
-  const bool ok = !ms.abort_flag;
-  if (ok) {
-    const float sig = exp2f(static_cast<float>(ms.sigma));
+  if (!ms.abort_flag) {
+    const float sig = exp2f(static_cast<float>(sigma_prev));
     // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane
 #pragma unroll 1
     for (int cc = 0; cc < 2; ++cc) {
@@ -634,8 +766,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(DecodeArgs
 }
 
 }  // namespace
-
-int decode_tc_smem_bytes() { return kSmemTC; }
 
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(mla_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTC);

@@ -28,15 +28,31 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 // Descriptors
 // ---------------------------------------------------------------------------
 
-// Shared-memory matrix descriptor, SWIZZLE_NONE, sm100 version bits.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+enum : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
+
+// Shared-memory matrix descriptor (sm100 version bits, base offset 0).
+// Swizzled operands must start their swizzle atoms on an atom-size boundary
+// (1024 B for 128B swizzle, 512 B for 64B); a K-major start address may
+// advance inside the atom's first row (K steps of 32 B).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout = kSwizzleNone) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1u) << 46;  // descriptor version for tcgen05
-  // base offset 0, lbo mode 0, layout type 0 (SWIZZLE_NONE)
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` inside a 128B-swizzled
+// atom (8 rows x 128 B): chunk index XOR (row mod 8).
+__host__ __device__ constexpr uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
+  return (row & 7u) * 128u + ((chunk ^ (row & 7u)) & 7u) * 16u;
+}
+// Same inside a 64B-swizzled atom (8 rows x 64 B): chunk index XOR ((row / 2) mod 4).
+__host__ __device__ constexpr uint32_t sw64_offset(uint32_t row, uint32_t chunk) {
+  return (row & 7u) * 64u + ((chunk ^ ((row >> 1) & 3u)) & 3u) * 16u;
 }
 
 enum : uint32_t {
@@ -108,6 +124,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
@@ -122,6 +147,16 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// A operand from TMEM (lane = row m, 32-bit column = two consecutive 16-bit K elements).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void mma_f8f6f4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,

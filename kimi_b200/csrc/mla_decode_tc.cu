@@ -8,17 +8,16 @@
 //
 // One CTA = a sequence, a range of its pages, up to 64 heads.
 //   * The cache is consumed in tiles of 128 tokens (two pages).  Tokens sit on
-//     the MMA's M dimension (M = 128) and heads on N ("swap AB"), so 64 heads
-//     fill a full-rate tcgen05 MMA.
+//     the MMA's M dimension (M = 128) and heads on N ("swap AB").
 //   * Each latent element is dequantised ONCE per tile into an 8-bit tile V''
-//     in shared memory: e2m1 -> f16 (cvt.rn.f16x2.e2m1x2), times the e8m0
-//     scale relative to a reference 2^sigma (one f16x2 multiply), then the
-//     high byte of the f16, which is the e5m2 encoding of the same value
-//     (e2m1 * 2^k has one mantissa bit, so it is exact while the exponent is
-//     in e5m2's range; sigma follows the tile maxima, see below).  V'' is
-//     stored in 128B-swizzled atoms (8 tokens x 128 latent bytes) and read by
-//     the tensor core twice: K-major as the A operand of S^T = V'' . Q''^T and
-//     MN-major as the A operand of O^T = V''^T . P''^T.
+//     in shared memory: the e2m1 code times its e8m0 scale relative to a
+//     reference 2^sigma, written as e5m2 (e2m1 * 2^k has one mantissa bit, so
+//     the value is exact while the exponent is in e5m2's range; sigma follows
+//     the tile maxima, see below).  The conversion is a byte permute through a
+//     two-register table per 32-element group (no conversion instructions).
+//     V'' sits in 128B-swizzled atoms (8 tokens x 128 latent bytes) and is read
+//     by the tensor core twice: K-major as the A operand of S^T = V'' . Q''^T
+//     and MN-major as the A operand of O^T = V''^T . P''^T.
 //   * q_nope is split into two e4m3 terms with a per-head power-of-two scale
 //     a_h (q / a_h = hi + lo), stacked as one N = 128 B operand: bf16-level
 //     accuracy for QK^T at fp8 tensor rate.  q_pe . k_pe is a bf16 MMA whose
@@ -35,12 +34,20 @@
 //     k_pe double buffer [192,256), O^T [256,512) as four 128-row latent
 //     chunks of 64 head columns.
 //
-// Pipeline: warps 0-7 alternate the softmax of tile j (S(j)) and the dequant
-// of tile j+1 (D(j+1)) into the other V'' buffer; warp 8 owns TMEM and issues
-// QK(j+1) and PV(j) as soon as their inputs are ready, so the tensor core
-// overlaps the CUDA-core work.  Every mbarrier wait is bounded; on timeout
-// the CTA records the failure and all threads still meet at the same final
-// barrier.
+// Warp roles (16 warps, 512 threads):
+//   warps 0-7   softmax: S(j) -> P''(j), O rescales, the epilogue;
+//   warps 8-11  loaders: global -> registers one tile ahead, then V''(j) and
+//               k_pe(j) (one TMEM lane quadrant each);
+//   warp 12     allocates TMEM and issues QK(j) (+ the RoPE MMAs);
+//   warps 13-14 issue PV(j) (latent chunks {0,1} and {2,3}): a single thread
+//               issues one tcgen05.mma every ~64 cycles while the N = 64 PV
+//               MMAs take ~48, so PV needs two issuers to keep the tensor pipe
+//               fed; warp 15 only completes the warpgroup.
+// V'' and k_pe are double-buffered, so QK(j+1) overlaps softmax(j) and the
+// loaders' D(j+2) overlaps PV(j+1).  Every mbarrier wait is bounded; a wait
+// that gives up sets a shared abort word that every other wait polls, each
+// role leaves its loop collectively, the issuers drain their MMAs and TMEM is
+// freed as usual.
 #include <cstddef>
 
 #include <cuda_fp16.h>
@@ -55,12 +62,28 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kNH = 64;             // heads per CTA (N of the MMAs)
-constexpr int kCompute = 256;       // dequant + softmax threads
-constexpr int kThreadsTC = kCompute + 32;
+constexpr int kNH = 64;               // heads per CTA (N of the MMAs)
+constexpr int kSoftmaxWarps = 8;
+constexpr int kLoaderWarp0 = 8;       // warps 8..11
+constexpr int kWarpQK = 12;
+constexpr int kWarpPV0 = 13;          // warps 13, 14 (warp 15 idles)
+constexpr int kPvIssuers = 2;
+constexpr int kThreadsTC = 512;
+constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
+constexpr int kLoaderThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColSpe = 128, kColKpe = 192, kColO = 256;
 constexpr uint32_t kPollLimit = 1u << 22;
+// Register budgets: 512 threads launch with 128 registers each (65536).  The
+// loader warpgroup takes 184, the issuer warpgroup gives back down to 72:
+// 256 * 128 + 128 * 184 + 128 * 72 = 65536.
+constexpr uint32_t kLoaderRegs = 184;
+constexpr uint32_t kIssuerRegs = 72;
+static_assert(256 * 128 + 128 * kLoaderRegs + 128 * kIssuerRegs <= kThreadsTC * 128, "register split");
+
+// Named barriers (0 is __syncthreads)
+constexpr int kBarSoftmax = 1;
+constexpr int kBarLoader = 2;
 
 // Shared memory (bytes).  Core matrix (r, c) of an operand lives at
 // r * row_stride + c * 128, 16 bytes per row inside the core.
@@ -80,14 +103,16 @@ constexpr int kPRow = 4 * 128;
 constexpr int kOffMisc = kOffPlo + 8192;
 
 struct Misc {
-  uint64_t mb_s;      // QK(j) complete (tcgen05.commit)
-  uint64_t mb_o;      // PV(j) complete (tcgen05.commit)
-  uint64_t mb_vfull;  // V''(j) and k_pe(j) written (8 warp arrivals)
-  uint64_t mb_sfree;  // S(j) read out of TMEM (8 warp arrivals)
-  uint64_t mb_pfull;  // P''(j) written, O rescaled (8 warp arrivals)
+  uint64_t mb_vfull[2];   // V''/k_pe buffer b written (4 loader warp arrivals)
+  uint64_t mb_pvdone[2];  // PV of the tile in buffer b complete (one commit per PV issuer)
+  uint64_t mb_sfull;      // QK(j) complete (tcgen05.commit)
+  uint64_t mb_sfree;      // S(j) read out of TMEM (8 softmax warp arrivals)
+  uint64_t mb_pfull;      // P''(j) written, O rescaled (8 softmax warp arrivals)
+  uint64_t mb_drain;      // each issuer's last commit (1 + kPvIssuers arrivals)
   uint32_t tmem_base;
   int abort_flag;
-  int tile_smax[2];   // max e8m0 byte of the tile being dequantised (reset by parity)
+  int tile_smax[4];       // max e8m0 byte of tile j in slot j % 4 (reset two tiles ahead)
+  int sig[2];             // reference exponent sigma of the tile in V'' buffer b
   alignas(16) float ac[kNH];  // a_h * sm_scale * log2(e)   (read as float4)
   alignas(16) float R[kNH];   // per-head exp2 offset, log2 units (read as float4)
   float alpha[kNH];   // O rescale factors of the current event
@@ -98,7 +123,7 @@ constexpr int kSmemTC = kOffMisc + static_cast<int>(sizeof(Misc));
 static_assert(kSmemTC <= 232448, "shared memory budget");
 static_assert(kOffMisc % 16 == 0 && offsetof(Misc, ac) % 16 == 0 && offsetof(Misc, R) % 16 == 0,
               "per-head arrays are read with 16-byte vector loads");
-static_assert(offsetof(Misc, mb_s) % 8 == 0 && offsetof(Misc, mb_pfull) % 8 == 0, "mbarriers are 8-byte aligned");
+static_assert(offsetof(Misc, mb_vfull) % 8 == 0 && offsetof(Misc, mb_drain) % 8 == 0, "mbarriers are 8-byte aligned");
 
 __device__ __forceinline__ uint8_t* smem_base() {
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
@@ -109,16 +134,16 @@ __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
-// Barrier over the compute threads that also ORs a predicate across them.
-__device__ __forceinline__ bool compute_bar_or(bool pred) {
+// Barrier over `count` threads that also ORs a predicate across them.
+__device__ __forceinline__ bool bar_or(int id, int count, bool pred) {
   uint32_t out;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 4, 256, p;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}\n"
       : "=r"(out)
-      : "r"(pred ? 1u : 0u)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
       : "memory");
   return out != 0;
 }
@@ -127,32 +152,43 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(mbar)) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_test(uint64_t* mbar, uint32_t parity) {
-  uint32_t ok;
+// Guarded loads: the predicate sits on the load itself and the destination
+// keeps its preset value when it is false.  (A load followed by a select on
+// the guard would make the select, and so the thread, wait for the data.)
+__device__ __forceinline__ uint4 ldg_stream_if(const void* p, bool pred) {
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(mbar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %5, 0;\n\t"
+      "@p ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n\t}\n"
+      : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+      : "l"(p), "r"(pred ? 1u : 0u));
   return v;
 }
 
-__device__ __forceinline__ uint4 ldg_cached(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+__device__ __forceinline__ uint32_t ldg_u8_if(const uint8_t* p, bool pred) {
+  uint32_t v = 0u;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+      "@p ld.global.nc.u8 %0, [%1];\n\t}\n"
+      : "+r"(v)
+      : "l"(p), "r"(pred ? 1u : 0u));
   return v;
+}
+
+__device__ __forceinline__ int ldg_s32_or(const int32_t* p, bool pred, int fallback) {
+  int v = fallback;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+      "@p ld.global.nc.s32 %0, [%1];\n\t}\n"
+      : "+r"(v)
+      : "l"(p), "r"(pred ? 1u : 0u));
+  return v;
+}
+
+// Bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2
+// without waiting; the loads that follow hit in L2.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -177,28 +213,36 @@ __device__ __forceinline__ void e5m2_tables(int k, uint32_t& lut_lo, uint32_t& l
   lut_hi = 0x46444240u + 0x04040404u * static_cast<uint32_t>(k);
 }
 
-// Eight e2m1 values (one u32 of packed nibbles, element 2j in the low nibble
-// of byte j) -> eight e5m2 bytes in element order.
-__device__ __forceinline__ void e2m1x8_to_e5m2(uint32_t w, uint32_t lut_lo, uint32_t lut_hi, uint32_t& o0,
-                                               uint32_t& o1) {
-  const uint32_t m0 = __byte_perm(lut_lo, lut_hi, w & 0x7777u);          // magnitudes of elements 0..3
-  const uint32_t m1 = __byte_perm(lut_lo, lut_hi, (w >> 16) & 0x7777u);  // elements 4..7
-  const uint32_t y0 = __byte_perm(w, 0u, 0x1100);                        // bytes b0 b0 b1 b1
-  const uint32_t y1 = __byte_perm(w, 0u, 0x3322);                        // bytes b2 b2 b3 b3
-  // sign of element 2j sits in bit 3 of byte j, of element 2j+1 in bit 7
-  o0 = m0 | ((y0 << 4) & 0x00800080u) | (y0 & 0x80008000u);
-  o1 = m1 | ((y1 << 4) & 0x00800080u) | (y1 & 0x80008000u);
+// prmt.b32 (default mode): byte n of the result is byte (sel_n & 7) of {a, b};
+// when sel_n & 8 it is that byte's sign bit replicated over all eight bits.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
 }
 
-// Sixteen packed nibble bytes (32 elements of one e8m0 group) with shift k ->
-// 32 e5m2 bytes (two 16-byte rows of V'').
-__device__ __forceinline__ void group_to_e5m2(const uint4& nib, int k, uint4& out0, uint4& out1) {
-  uint32_t lo, hi;
-  e5m2_tables(k, lo, hi);
-  e2m1x8_to_e5m2(nib.x, lo, hi, out0.x, out0.y);
-  e2m1x8_to_e5m2(nib.y, lo, hi, out0.z, out0.w);
-  e2m1x8_to_e5m2(nib.z, lo, hi, out1.x, out1.y);
-  e2m1x8_to_e5m2(nib.w, lo, hi, out1.z, out1.w);
+// Eight e2m1 values (one u32 of packed nibbles, element 2j in the low nibble
+// of byte j) -> eight e5m2 bytes in element order: nine instructions.
+__device__ __forceinline__ void e2m1x8_to_e5m2(uint32_t w, uint32_t lut_lo, uint32_t lut_hi, uint32_t& o0,
+                                               uint32_t& o1) {
+  const uint32_t wm = w & 0x77777777u;                 // magnitude codes (selector bit 3 clear)
+  const uint32_t m0 = prmt(lut_lo, lut_hi, wm);        // elements 0..3 (low four selector nibbles)
+  const uint32_t m1 = prmt(lut_lo, lut_hi, wm >> 16);  // elements 4..7
+  // sign of element 2j is bit 3 of byte j (bit 7 of byte j of w << 4), of
+  // element 2j + 1 bit 7 of byte j: replicate them into sign masks
+  const uint32_t w4 = w << 4;
+  const uint32_t s0 = prmt(w4, w, 0xD9C8u);
+  const uint32_t s1 = prmt(w4, w, 0xFBEAu);
+  o0 = m0 | (s0 & 0x80808080u);
+  o1 = m1 | (s1 & 0x80808080u);
+}
+
+// Eight nibble bytes (16 elements) with shift k -> 16 e5m2 bytes.
+__device__ __forceinline__ uint4 half_group_to_e5m2(uint32_t w0, uint32_t w1, uint32_t lut_lo, uint32_t lut_hi) {
+  uint4 o;
+  e2m1x8_to_e5m2(w0, lut_lo, lut_hi, o.x, o.y);
+  e2m1x8_to_e5m2(w1, lut_lo, lut_hi, o.z, o.w);
+  return o;
 }
 
 // p (two floats) -> e4m3 hi and e4m3 residual, through f16 (exact residual).
@@ -228,62 +272,75 @@ __device__ __forceinline__ int tile_valid(const WorkItem& w, int tile) {
   return max(0, min(min(kPageSize * 2, w.n_tok - p0 * kPageSize), (w.p_end - p0) * kPageSize));
 }
 
-// Raw data of one tile held by one thread.  Latent nibbles follow the loader
-// mapping: warp w covers tokens 16w..16w+15; in load i (0..7) lanes 0-15 read
-// the sixteen 16-byte chunks (= e8m0 groups) of token 16w + 2i and lanes 16-31
-// those of token 16w + 2i + 1, so every load instruction reads four whole
-// 128-byte lines.  A thread thus holds group g = lane % 16 of eight tokens,
-// with the matching scale bytes.  RoPE follows the TMEM mapping (token st,
-// bytes [64 hf, 64 hf + 64)).
-struct TileRegs {
-  uint4 nib[8];
-  uint32_t sb[8];         // scale byte of group g for each of the eight tokens
-  uint4 pe[4];
+// Raw data of one tile held by one loader thread (quadrant q = its warp - 8,
+// tokens 32q .. 32q + 31 of the tile, all in one page).  Latent nibbles: lane
+// l holds e8m0 group g = (l % 4) + 4 (l / 8) (one 16-byte chunk) of token
+// 32q + 2i + e, e = (l / 4) % 2, for i = 0..15, with the matching scale bytes.
+// Every load instruction reads two whole token rows (four 128-byte lines), and
+// each 8-lane phase of a V'' store covers two tokens of opposite parity x four
+// groups: eight distinct 16-byte bank groups of the swizzled atoms.  RoPE: in
+// load k (0..7) lane l reads 16-byte chunk l % 8 of token 32q + 4k + l / 8
+// (line-coalesced); the loader transposes it to one token per lane.
+struct RawTile {
+  uint4 nib[16];
+  uint32_t sb[16];
+  uint4 pe[8];
   int nvalid;
-  int page_next[2];       // page ids of the tile loaded next (fetched one tile ahead)
+  int page_next[2];  // page ids of the tile loaded next (fetched one tile ahead)
+  int page_pf[2];    // page ids of the tile prefetched into L2 next (loader thread 0 only)
 };
+
+// L2 prefetch distance in tiles: the register loads of tile j find its pages
+// in L2, fetched while tiles j - kPrefetchTiles .. j - 1 were processed.
+constexpr int kPrefetchTiles = 3;
 
 __device__ __forceinline__ void fetch_pages(const DecodeArgs& a, const WorkItem& w, int tile, int (&pg)[2]) {
 #pragma unroll
   for (int slot = 0; slot < 2; ++slot) {
     const int p = w.p_begin + 2 * tile + slot;
-    pg[slot] = p < w.p_end ? __ldg(a.kv_indices + w.page_lo + p) : -1;
+    const bool in_range = p < w.p_end;
+    pg[slot] = ldg_s32_or(a.kv_indices + w.page_lo + (in_range ? p : 0), in_range, -1);
   }
 }
 
-__device__ __forceinline__ void load_tile(const DecodeArgs& a, const WorkItem& w, int tile, int warp, int lane,
-                                          int st, int hf, TileRegs& r) {
+__device__ __forceinline__ void load_tile(const DecodeArgs& a, const WorkItem& w, int tile, int q, int lane,
+                                          RawTile& r) {
   const int nvalid = tile_valid(w, tile);
   r.nvalid = nvalid;
-  const int pg[2] = {r.page_next[0], r.page_next[1]};
-  const int e = lane >> 4, g = lane & 15;
-  const int slot = warp >> 2;  // tokens 16w..16w+15 lie in one page
-  const int page = (pg[slot] >= 0 && pg[slot] < a.num_pages) ? pg[slot] : -1;
+  const int pid = (q >> 1) ? r.page_next[1] : r.page_next[0];  // (a select keeps page_next in registers)
+  const int page = (pid >= 0 && pid < a.num_pages) ? pid : -1;
   const uint8_t* pbase = a.kv_buffer + static_cast<int64_t>(page < 0 ? 0 : page) * kPageBytes;
   const uint8_t* sbase = a.kv_scales + static_cast<int64_t>(page < 0 ? 0 : page) * kPageScaleBytes;
+  const int e = (lane >> 2) & 1, g = (lane & 3) | ((lane >> 3) << 2);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int tk = 16 * warp + 2 * i + e;
-    if (page >= 0 && tk < nvalid) {
-      r.nib[i] = ldg_stream(pbase + (tk & 63) * kTokenBytes + 16 * g);
-      r.sb[i] = __ldg(sbase + (tk & 63) * kScaleBytes + g);
-    } else {
-      r.nib[i] = make_uint4(0, 0, 0, 0);
-      r.sb[i] = 0u;
-    }
+  for (int i = 0; i < 16; ++i) {
+    const int tk = 32 * q + 2 * i + e;
+    r.nib[i] = ldg_stream_if(pbase + (tk & 63) * kTokenBytes + 16 * g, page >= 0 && tk < nvalid);
   }
-  const int pslot = st >> 6;
-  const int ppage = (pg[pslot] >= 0 && pg[pslot] < a.num_pages && st < nvalid) ? pg[pslot] : -1;
-  if (ppage >= 0) {
-    const uint8_t* row = a.kv_buffer + static_cast<int64_t>(ppage) * kPageBytes + (st & 63) * kTokenBytes +
-                         kNibbleBytes + 64 * hf;
+  // (each byte stays in its own register: combining them here would wait for the loads)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) r.pe[k] = ldg_cached(row + 16 * k);
-  } else {
+  for (int i = 0; i < 16; ++i) {
+    const int tk = 32 * q + 2 * i + e;
+    r.sb[i] = ldg_u8_if(sbase + (tk & 63) * kScaleBytes + g, page >= 0 && tk < nvalid);
+  }
+  // RoPE, line-coalesced: in load k lane l reads 16-byte chunk l % 8 of token 32q + 4k + l / 8
 #pragma unroll
-    for (int k = 0; k < 4; ++k) r.pe[k] = make_uint4(0, 0, 0, 0);
+  for (int k = 0; k < 8; ++k) {
+    const int tk = 32 * q + 4 * k + (lane >> 3);
+    r.pe[k] = ldg_stream_if(pbase + (tk & 63) * kTokenBytes + kNibbleBytes + 16 * (lane & 7), page >= 0 && tk < nvalid);
   }
   fetch_pages(a, w, tile + 1, r.page_next);
+}
+
+// Loader thread 0: prefetch the pages (cache rows and scales) of one tile into L2.
+__device__ __forceinline__ void prefetch_tile(const DecodeArgs& a, const int (&pg)[2]) {
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    if (pg[slot] >= 0 && pg[slot] < a.num_pages) {
+      prefetch_l2(a.kv_buffer + static_cast<int64_t>(pg[slot]) * kPageBytes, kPageBytes);
+      prefetch_l2(a.kv_scales + static_cast<int64_t>(pg[slot]) * kPageScaleBytes, kPageScaleBytes);
+    }
+  }
 }
 
 // Transpose-reduce (max or sum) of 32 per-lane values over the warp: lane j
@@ -308,143 +365,372 @@ __device__ __forceinline__ void record_status(const DecodeArgs& a, int bits) {
   if (a.status) atomicOr(a.status, bits);
 }
 
-__device__ __forceinline__ bool wait_or_abort(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit) {
-  if (mbar_wait_bounded(mb, parity, kPollLimit)) return true;
-  atomicExch(&ms.abort_flag, 1);
-  record_status(a, bit);
+// Per-thread bounded wait; on give-up records the failure and raises the abort word.
+__device__ __forceinline__ bool wait_phase(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit) {
+  if (mbar_wait_or_abort(mb, parity, kPollLimit, &ms.abort_flag)) return true;
+  if (atomicExch(&ms.abort_flag, 1) == 0) record_status(a, bit);
   return false;
 }
 
+// Warp-uniform bounded wait: lane 0 polls, the warp gets its verdict.
+__device__ __forceinline__ bool warp_wait(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit,
+                                          int lane) {
+  bool ok = true;
+  if (lane == 0) ok = wait_phase(mb, parity, ms, a, bit);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 // ---------------------------------------------------------------------------
-// MMA issuer (warp 8, lane 0 issues)
+// Issuers (warps 12..15; lane 0 issues)
 // ---------------------------------------------------------------------------
-__device__ void mma_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int lane, const DecodeArgs& a) {
+__device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int lane, const DecodeArgs& a) {
   const uint32_t id_qk = instr_desc(kFmtE5M2, kFmtE4M3, false, false, 128, 128);
   const uint32_t id_pe = instr_desc(kFmtBF16, kFmtBF16, false, false, 128, 64);
-  const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, 64);
   const uint32_t sQ = smem_addr(sm + kOffQ), sQpe = smem_addr(sm + kOffQpe);
+  for (int j = 0; j < n_tiles; ++j) {
+    // QK(j) needs V''(j)/k_pe(j) written and S(j-1) read out of TMEM (single S buffer)
+    if (!warp_wait(&ms.mb_vfull[j & 1], static_cast<uint32_t>((j >> 1) & 1), ms, a, 16, lane)) break;
+    if (j > 0 && !warp_wait(&ms.mb_sfree, static_cast<uint32_t>((j - 1) & 1), ms, a, 16, lane)) break;
+    fence_after_sync();
+    if (lane == 0) {
+      const uint32_t sV = smem_addr(sm + kOffV + (j & 1) * kVBytes);
+      // The 16 latent MMAs chain on one accumulator; the 4 RoPE MMAs (own
+      // accumulator) are interleaved so they fill the chain's latency.
+      const uint32_t kpe = tmem + kColKpe + 32 * (j & 1);
+#pragma unroll 1
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t koff = (k >> 2) * kVCol + (k & 3) * 32;
+        mma_f8f6f4_ss(tmem + kColS, smem_desc(sV + koff, 16, 1024, kSwizzle128B),
+                      smem_desc(sQ + koff, 16, 1024, kSwizzle128B), id_qk, k > 0);
+        if (k < 4) mma_f16_ts(tmem + kColSpe, kpe + 8 * k, smem_desc(sQpe + k * 256, 128, kPeRow), id_pe, k > 0);
+      }
+      mma_commit(&ms.mb_sfull);
+    }
+    __syncwarp();
+  }
+}
+
+// PV issuer p owns latent chunks 2p and 2p + 1.
+__device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int lane, int p, const DecodeArgs& a) {
+  const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, 64);
   const uint32_t sP = smem_addr(sm + kOffP), sPlo = smem_addr(sm + kOffPlo);
-  int qk_next = 0, pv_next = 0;
-  uint32_t idle = 0;
-  while (pv_next < n_tiles) {
-    bool progressed = false;
-    // QK(j) needs V''(j) written and S(j-1) read out of TMEM (single S buffer).
-    if (qk_next < n_tiles && qk_next <= pv_next + 1 && mbar_test(&ms.mb_vfull, qk_next & 1) &&
-        (qk_next == 0 || mbar_test(&ms.mb_sfree, (qk_next - 1) & 1))) {
-      fence_after_sync();
-      if (lane == 0) {
-        const uint32_t sV = smem_addr(sm + kOffV + (qk_next & 1) * kVBytes);
-        // The 16 latent MMAs chain on one accumulator; the 4 RoPE MMAs (own
-        // accumulator) are interleaved so they fill the chain's latency.
-        const uint32_t kpe = tmem + kColKpe + 32 * (qk_next & 1);
+  const int c0 = 2 * p;
+  const int c1 = 2 * p + 2;
+  for (int j = 0; j < n_tiles; ++j) {
+    // PV(j) needs P''(j) (written after PV(j-1) completed and O was rescaled)
+    if (!warp_wait(&ms.mb_pfull, static_cast<uint32_t>(j & 1), ms, a, 32, lane)) break;
+    fence_after_sync();
+    if (lane == 0) {
+      const uint32_t sV = smem_addr(sm + kOffV + (j & 1) * kVBytes);
 #pragma unroll 1
-        for (int k = 0; k < 16; ++k) {
-          const uint32_t koff = (k >> 2) * kVCol + (k & 3) * 32;
-          mma_f8f6f4_ss(tmem + kColS, smem_desc(sV + koff, 16, 1024, kSwizzle128B),
-                        smem_desc(sQ + koff, 16, 1024, kSwizzle128B), id_qk, k > 0);
-          if (k < 4)
-            mma_f16_ts(tmem + kColSpe, kpe + 8 * k, smem_desc(sQpe + k * 256, 128, kPeRow), id_pe, k > 0);
-        }
-        mma_commit(&ms.mb_s);
+      for (int k = 0; k < 4; ++k) {
+        const uint64_t phi = smem_desc(sP + k * 4 * kPRow, kPRow, 128);
+        const uint64_t plo = smem_desc(sPlo + k * 4 * kPRow, kPRow, 128);
+        for (int c = c0; c < c1; ++c)
+          mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B), phi,
+                        id_pv, (j > 0 || k > 0) ? 1u : 0u);
+        for (int c = c0; c < c1; ++c)
+          mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B), plo,
+                        id_pv, 1u);
+      }
+      mma_commit(&ms.mb_pvdone[j & 1]);
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Loaders (warps 8..11): V''(j) and k_pe(j) from registers, then the next tile's loads
+// ---------------------------------------------------------------------------
+__device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w, int n_tiles, int q, int lane,
+                       const DecodeArgs& a) {
+  const int ltid = 32 * q + lane;
+  const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
+  const int e = (lane >> 2) & 1, g = (lane & 3) | ((lane >> 3) << 2);
+  RawTile r;
+  fetch_pages(a, w, 0, r.page_next);
+  if (ltid == 0) {
+    // tiles 1 .. kPrefetchTiles now; tile j + kPrefetchTiles when tile j is loaded
+    for (int t = 1; t <= kPrefetchTiles; ++t) {
+      fetch_pages(a, w, t, r.page_pf);
+      prefetch_tile(a, r.page_pf);
+    }
+    fetch_pages(a, w, kPrefetchTiles + 1, r.page_pf);
+  }
+  load_tile(a, w, 0, q, lane, r);
+  int prev_sigma = 0;
+  for (int j = 0; j < n_tiles; ++j) {
+    const int buf = j & 1;
+    // V'' buffer j & 1 (and its k_pe TMEM buffer) was last read by PV(j-2) / QK(j-2)
+    bool ok = true;
+    if (j >= 2) ok = warp_wait(&ms.mb_pvdone[buf], static_cast<uint32_t>(((j >> 1) - 1) & 1), ms, a, 64, lane);
+    // tile maximum of the e8m0 bytes (invalid tokens carry 0) -> reference exponent
+    uint32_t my_max = 0u;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) my_max = max(my_max, r.sb[i]);
+    my_max = __reduce_max_sync(0xffffffffu, my_max);
+    if (lane == 0) atomicMax(&ms.tile_smax[j & 3], static_cast<int>(my_max));
+    if (bar_or(kBarLoader, kLoaderThreads, !ok)) break;
+    const int smax = ms.tile_smax[j & 3];
+    int sigma;
+    if (j == 0) {
+      sigma = smax - 127 - 8;  // tile max maps to <= 6 * 2^8 in V''
+    } else {
+      const int kmax = smax - 127 - prev_sigma;
+      sigma = (kmax > 13 || kmax < -4) ? smax - 127 - 8 : prev_sigma;
+    }
+    if (ltid == 0) {
+      ms.tile_smax[(j + 2) & 3] = 0;
+      ms.sig[buf] = sigma;
+    }
+    prev_sigma = sigma;
+
+    // k_pe: token-per-lane transpose through this warp's own 4 KB of V'' (latent
+    // column 0, tokens 32q .. 32q + 31; overwritten by the V'' stores below).
+    // Chunk c of local token t sits at t * 128 + (c ^ (t & 7)) * 16: both the
+    // coalesced write and the per-token read touch eight distinct 16-byte bank groups.
+    uint32_t kpe[32];
+    {
+      uint8_t* scratch = sm + kOffV + buf * kVBytes + 4096 * q;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int t = 4 * k + (lane >> 3), c = lane & 7;
+        *reinterpret_cast<uint4*>(scratch + t * 128 + ((c ^ (t & 7)) * 16)) = r.pe[k];
       }
       __syncwarp();
-      ++qk_next;
-      progressed = true;
-    }
-    // PV(j) needs P''(j) (written after PV(j-1) completed and O was rescaled).
-    if (pv_next < qk_next && mbar_test(&ms.mb_pfull, pv_next & 1)) {
-      fence_after_sync();
-      if (lane == 0) {
-        const uint32_t sV = smem_addr(sm + kOffV + (pv_next & 1) * kVBytes);
-        // Consecutive MMAs go to different latent chunks (independent
-        // accumulators), so they pipeline instead of chaining.
-#pragma unroll 1
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t phi = smem_desc(sP + k * 4 * kPRow, kPRow, 128);
-          const uint64_t plo = smem_desc(sPlo + k * 4 * kPRow, kPRow, 128);
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B),
-                          phi, id_pv, (pv_next > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B),
-                          plo, id_pv, 1u);
-        }
-        mma_commit(&ms.mb_o);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = *reinterpret_cast<const uint4*>(scratch + lane * 128 + ((c ^ (lane & 7)) * 16));
+        kpe[4 * c] = v.x;
+        kpe[4 * c + 1] = v.y;
+        kpe[4 * c + 2] = v.z;
+        kpe[4 * c + 3] = v.w;
       }
       __syncwarp();
-      ++pv_next;
-      progressed = true;
+      // -> TMEM columns [kColKpe + 32 buf, +32) of this thread's TMEM lane (token 32q + lane)
+      tmem_st32(tmem + lane_base + kColKpe + 32 * buf, kpe);
     }
-    if (progressed) {
-      idle = 0;
-    } else if (++idle > kPollLimit || ms.abort_flag) {
-      atomicExch(&ms.abort_flag, 1);
-      record_status(a, 8);
+    // group g of sixteen tokens -> two 16-byte chunks (latent bytes 32g .. 32g + 31) each
+    uint8_t* vb = sm + kOffV + buf * kVBytes + (g >> 2) * kVCol;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int tk = 32 * q + 2 * i + e;
+      const uint32_t sbyte = r.sb[i];
+      uint32_t lo, hi;
+      e5m2_tables(static_cast<int>(sbyte) - 127 - sigma, lo, hi);
+      const uint4 nb = r.nib[i];
+      uint8_t* atom = vb + (tk >> 3) * 1024;
+      *reinterpret_cast<uint4*>(atom + sw128_offset(tk & 7, (2 * g) & 7)) = half_group_to_e5m2(nb.x, nb.y, lo, hi);
+      *reinterpret_cast<uint4*>(atom + sw128_offset(tk & 7, (2 * g + 1) & 7)) = half_group_to_e5m2(nb.z, nb.w, lo, hi);
+    }
+    tmem_st_wait();
+    fence_proxy_async_smem();
+    fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms.mb_vfull[buf]);
+    if (j + 1 < n_tiles) {
+      if (ltid == 0) {
+        prefetch_tile(a, r.page_pf);  // tile j + 1 + kPrefetchTiles (ids fetched one tile ago)
+        fetch_pages(a, w, j + 2 + kPrefetchTiles, r.page_pf);
+      }
+      load_tile(a, w, j + 1, q, lane, r);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Softmax warps (0..7) and the epilogue
+// ---------------------------------------------------------------------------
+__device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w, int n_tiles, int warp, int lane,
+                        float c_log2, const DecodeArgs& a) {
+  const int tid = threadIdx.x;
+  const int q = warp & 3;                  // TMEM lane quadrant
+  const int hf = warp >> 2;                // heads 32 hf .. 32 hf + 31
+  const int st = 32 * q + lane;            // softmax token
+  const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
+  const bool direct = a.num_splits == 1;
+
+  float l_part[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
+  int sigma_prev = 0;
+  bool aborted = false;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const uint32_t par = static_cast<uint32_t>(tile & 1);
+    // V''(j) written (for sigma of the tile), QK(j) complete
+    bool ok = warp_wait(&ms.mb_vfull[tile & 1], static_cast<uint32_t>((tile >> 1) & 1), ms, a, 1, lane) &&
+              warp_wait(&ms.mb_sfull, par, ms, a, 1, lane);
+    fence_after_sync();
+    float t[32];
+    if (ok) {
+      uint32_t s_hi[32], s_lo[32];
+      tmem_ld32(tmem + lane_base + kColS + 32 * hf, s_hi);
+      tmem_ld32(tmem + lane_base + kColS + 64 + 32 * hf, s_lo);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(s_hi[j]) + __uint_as_float(s_lo[j]);
+      uint32_t s_pe[32];
+      tmem_ld32(tmem + lane_base + kColSpe + 32 * hf, s_pe);
+      tmem_ld_wait();
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ms.mb_sfree);
+      const int sigma = ms.sig[tile & 1];
+      const float sig = __uint_as_float(static_cast<uint32_t>(min(max(sigma + 127, 1), 254)) << 23);
+      const bool tvalid = st < tile_valid(w, tile);
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 ac4 = *reinterpret_cast<const float4*>(&ms.ac[32 * hf + j]);
+        const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[32 * hf + j]);
+        const float acv[4] = {ac4.x, ac4.y, ac4.z, ac4.w};
+        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float base = fmaf(__uint_as_float(s_pe[j + u]), c_log2, -rv[u]);
+          t[j + u] = tvalid ? fmaf(t[j + u], acv[u] * sig, base) : -CUDART_INF_F;
+        }
+      }
+      // PV(j-1) must be complete before O is rescaled or P'' is overwritten
+      if (tile > 0)
+        ok = warp_wait(&ms.mb_pvdone[(tile - 1) & 1], static_cast<uint32_t>(((tile - 1) >> 1) & 1), ms, a, 2, lane);
+    }
+    if (bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
+      aborted = true;
       break;
     }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Dequant of one tile into a V'' buffer and a k_pe TMEM buffer
-// ---------------------------------------------------------------------------
-// Returns the reference exponent sigma chosen for the tile (identical in every thread).
-__device__ __forceinline__ int dequant_tile(uint8_t* sm, Misc& ms, uint32_t tmem, uint32_t lane_base, int tile,
-                                            int prev_sigma, const TileRegs& r, int warp, int lane, int hf, int tid) {
-  const int buf = tile & 1;
-  // tile maximum of the e8m0 bytes (invalid tokens carry 0) -> reference exponent
-  uint32_t my_max = 0u;
+    fence_after_sync();
+    // rescale event: first tile, a score above R + 8.5, or a new sigma
+    float tmaxv = -CUDART_INF_F;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) my_max = max(my_max, r.sb[i]);
-  my_max = __reduce_max_sync(0xffffffffu, my_max);
-  if (lane == 0) atomicMax(&ms.tile_smax[buf], static_cast<int>(my_max));
-  named_bar(4, kCompute);
-  const int smax = ms.tile_smax[buf];
-  int sigma;
-  if (tile == 0) {
-    sigma = smax - 127 - 8;  // tile max maps to <= 6 * 2^8 in V''
-  } else {
-    const int kmax = smax - 127 - prev_sigma;
-    sigma = (kmax > 13 || kmax < -4) ? smax - 127 - 8 : prev_sigma;
-  }
-  if (tid == 0) ms.tile_smax[buf ^ 1] = 0;
-
-  // group g of eight tokens -> two 16-byte chunks (latent bytes 32g .. 32g + 31) each
-  const int e = lane >> 4, g = lane & 15;
-  uint8_t* vb = sm + kOffV + buf * kVBytes + (g >> 2) * kVCol;
+    for (int j = 0; j < 32; ++j) tmaxv = fmaxf(tmaxv, t[j]);
+    const int sigma_cur = ms.sig[tile & 1];
+    const bool need = bar_or(kBarSoftmax, kSoftmaxThreads, tile == 0 || tmaxv > 8.5f || sigma_cur != sigma_prev);
+    if (need) {
+      float v[32];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int tk = 16 * warp + 2 * i + e;
-    const uint32_t sbyte = r.sb[i];
-    uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
-    if (tk < r.nvalid) group_to_e5m2(r.nib[i], static_cast<int>(sbyte) - 127 - sigma, o0, o1);
-    uint8_t* atom = vb + (tk >> 3) * 1024;
-    *reinterpret_cast<uint4*>(atom + sw128_offset(tk & 7, (2 * g) & 7)) = o0;
-    *reinterpret_cast<uint4*>(atom + sw128_offset(tk & 7, (2 * g + 1) & 7)) = o1;
-  }
-  // k_pe -> TMEM columns [kColKpe + 32 buf + 16 hf, +16) of this thread's TMEM lane
-  {
-    uint32_t v[16];
+      for (int j = 0; j < 32; ++j) v[j] = t[j];
+      ms.red[q][32 * hf + lane] = warp_transpose_reduce<true>(v, lane);  // tile max of x - R_old
+      named_bar(kBarSoftmax, kSoftmaxThreads);
+      if (tid < kNH) {
+        const float tm = fmaxf(fmaxf(ms.red[0][tid], ms.red[1][tid]), fmaxf(ms.red[2][tid], ms.red[3][tid]));
+        // raise R so that this tile's max maps to 2^4 (only raise; the first tile sets it)
+        const float shift = tile == 0 ? tm - 4.0f : fmaxf(tm - 4.0f, 0.0f);
+        const float dshift = fmaxf(shift, -1e30f);
+        ms.R[tid] += dshift;
+        ms.beta[tid] = tile == 0 ? 1.0f : ex2(-dshift);
+        ms.alpha[tid] = tile == 0 ? 1.0f : ex2(-dshift + static_cast<float>(sigma_prev - sigma_cur));
+        ms.red[0][tid] = dshift;  // reused below as the per-head shift of t
+      }
+      named_bar(kBarSoftmax, kSoftmaxThreads);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v[4 * k] = r.pe[k].x;
-      v[4 * k + 1] = r.pe[k].y;
-      v[4 * k + 2] = r.pe[k].z;
-      v[4 * k + 3] = r.pe[k].w;
+      for (int j = 0; j < 32; ++j) t[j] -= ms.red[0][32 * hf + j];
+      if (tile > 0) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) l_part[j] *= ms.beta[32 * hf + j];
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * hf + cc;
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t vv[32];
+            const uint32_t ta = tmem + lane_base + kColO + 64 * c + 32 * hh;
+            tmem_ld32(ta, vv);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
+            tmem_st32(ta, vv);
+          }
+        }
+        tmem_st_wait();
+      }
+      // every thread has read red[0] and alpha before the next event overwrites them
+      named_bar(kBarSoftmax, kSoftmaxThreads);
     }
-    tmem_st16(tmem + lane_base + kColKpe + 32 * buf + 16 * hf, v);
-    tmem_st_wait();
+    sigma_prev = sigma_cur;
+
+    // ---- P'' = exp2(t) as e4m3 hi + residual, into the MN-major B operands ----
+    {
+      uint32_t pw[8], pl[8];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float p0 = ex2(t[j]);
+        const float p1 = ex2(t[j + 1]);
+        l_part[j] += p0;
+        l_part[j + 1] += p1;
+        uint16_t h8, l8;
+        split_e4m3x2(p0, p1, h8, l8);
+        if ((j & 2) == 0) {
+          pw[j / 4] = h8;
+          pl[j / 4] = l8;
+        } else {
+          pw[j / 4] |= static_cast<uint32_t>(h8) << 16;
+          pl[j / 4] |= static_cast<uint32_t>(l8) << 16;
+        }
+      }
+      const int prow = (st >> 3) * kPRow + (st & 7) * 16;
+      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf) * 128) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf + 1) * 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf) * 128) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf + 1) * 128) = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+    }
+    fence_proxy_async_smem();
+    fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms.mb_pfull);
   }
-  fence_proxy_async_smem();
-  fence_before_sync();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&ms.mb_vfull);
-  return sigma;
+
+  // ---------------- epilogue ----------------
+  if (!aborted) {
+    const bool ok = warp_wait(&ms.mb_pvdone[(n_tiles - 1) & 1], static_cast<uint32_t>(((n_tiles - 1) >> 1) & 1),
+                              ms, a, 4, lane);
+    aborted = bar_or(kBarSoftmax, kSoftmaxThreads, !ok);
+  }
+  if (aborted) return;
+  fence_after_sync();
+  {
+    const float s = warp_transpose_reduce<false>(l_part, lane);
+    ms.red[q][32 * hf + lane] = s;
+  }
+  named_bar(kBarSoftmax, kSoftmaxThreads);
+  if (tid < kNH) {
+    const float l = ms.red[0][tid] + ms.red[1][tid] + ms.red[2][tid] + ms.red[3][tid];
+    // output factor 2^sigma / l per head (alpha is free again)
+    ms.alpha[tid] = l > 0.f ? exp2f(static_cast<float>(sigma_prev)) / l : 0.f;
+    if (!direct && tid < w.heads_here) {
+      const int64_t row = (static_cast<int64_t>(w.b) * a.num_splits + w.split) * a.num_heads + w.head_base + tid;
+      a.partial_lse[row] = (ms.R[tid] + __log2f(l)) * kLn2;
+    }
+  }
+  named_bar(kBarSoftmax, kSoftmaxThreads);
+  // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane
+#pragma unroll 1
+  for (int cc = 0; cc < 2; ++cc) {
+    const int c = 2 * hf + cc;
+    const int d = 128 * c + 32 * q + lane;
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+      uint32_t vv[32];
+      tmem_ld32(tmem + lane_base + kColO + 64 * c + 32 * hh, vv);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int h = 32 * hh + j;
+        if (h < w.heads_here) {
+          const float val = __uint_as_float(vv[j]) * ms.alpha[h];
+          const int hq = w.head_base + h;
+          if (direct) {
+            a.o[w.b * a.o_stride_b + hq * a.o_stride_h + d] = __float2bfloat16_rn(val);
+          } else {
+            const int64_t row = (static_cast<int64_t>(w.b) * a.num_splits + w.split) * a.num_heads + hq;
+            a.partial_o[row * kLatent + d] = val;
+          }
+        }
+      }
+    }
+  }
 }
 
-// Nine warps put three on one SM sub-partition (16K registers): at most 168 registers per thread.
 __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __grid_constant__ DecodeArgs a) {
   uint8_t* sm = smem_base();
   Misc& ms = *reinterpret_cast<Misc*>(sm + kOffMisc);
@@ -483,30 +769,33 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __gr
   const float c_log2 = a.sm_scale * kLog2e;
 
   // ---------------- setup: TMEM, barriers, Q operands ----------------
-  if (warp == 8) {
+  if (warp == kWarpQK) {
     tmem_alloc(&ms.tmem_base, kTmemCols);
     if (lane == 0) {
-      mbar_init(&ms.mb_s, 1);
-      mbar_init(&ms.mb_o, 1);
-      mbar_init(&ms.mb_vfull, 8);
-      mbar_init(&ms.mb_sfree, 8);
-      mbar_init(&ms.mb_pfull, 8);
+      mbar_init(&ms.mb_vfull[0], 4);
+      mbar_init(&ms.mb_vfull[1], 4);
+      mbar_init(&ms.mb_pvdone[0], kPvIssuers);
+      mbar_init(&ms.mb_pvdone[1], kPvIssuers);
+      mbar_init(&ms.mb_sfull, 1);
+      mbar_init(&ms.mb_sfree, kSoftmaxWarps);
+      mbar_init(&ms.mb_pfull, kSoftmaxWarps);
+      mbar_init(&ms.mb_drain, 1 + kPvIssuers);
       fence_mbar_init();
       ms.abort_flag = 0;
-      ms.tile_smax[0] = 0;
-      ms.tile_smax[1] = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ms.tile_smax[i] = 0;
     }
-  } else {
+  } else if (warp < kSoftmaxWarps) {
     // 4 threads per head: part p handles latent [128p, 128p + 128) and RoPE [16p, 16p + 16).
     const int h = tid >> 2, part = tid & 3;
     const bool live = h < w.heads_here;
     const __nv_bfloat16* qrow = a.q + w.b * a.q_stride_b + (w.head_base + h) * a.q_stride_h;
+    // two passes over this thread's 128 latent values (the second hits in cache)
     float amax = 0.f;
-    uint4 qv[16];
-#pragma unroll
+#pragma unroll 4
     for (int k = 0; k < 16; ++k) {
-      qv[k] = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k) : make_uint4(0, 0, 0, 0);
-      const uint32_t ws[4] = {qv[k].x, qv[k].y, qv[k].z, qv[k].w};
+      const uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k) : make_uint4(0, 0, 0, 0);
+      const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(ws[j] << 16)), fabsf(__uint_as_float(ws[j] & 0xFFFF0000u))));
@@ -523,11 +812,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __gr
       ms.R[h] = 0.f;
     }
     uint8_t* qb = sm + kOffQ;
-#pragma unroll
+#pragma unroll 1
     for (int k = 0; k < 16; k += 2) {
       // 16 latent elements = one 16-byte core row of hi and of lo
       uint32_t hi_w[4], lo_w[4];
-      const uint32_t ws[8] = {qv[k].x, qv[k].y, qv[k].z, qv[k].w, qv[k + 1].x, qv[k + 1].y, qv[k + 1].z, qv[k + 1].w};
+      const uint4 v0 = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k) : make_uint4(0, 0, 0, 0);
+      const uint4 v1 = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k + 8) : make_uint4(0, 0, 0, 0);
+      const uint32_t ws[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float x0 = __uint_as_float(ws[2 * j] << 16) * inv_a;
@@ -562,207 +853,31 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __gr
   fence_after_sync();
   const uint32_t tmem = ms.tmem_base;
 
-  if (warp == 8) {
-    mma_issuer(sm, ms, tmem, n_tiles, lane, a);
-    fence_before_sync();
-    named_bar(3, kThreadsTC);  // epilogue done
+  if (warp >= kWarpQK) {
+    setmaxnreg_dec<kIssuerRegs>();
+    const bool issuer = warp < kWarpPV0 + kPvIssuers;
+    if (warp == kWarpQK)
+      qk_issuer(sm, ms, tmem, n_tiles, lane, a);
+    else if (issuer)
+      pv_issuer(sm, ms, tmem, n_tiles, lane, warp - kWarpPV0, a);
+    // drain: arrives once every MMA this thread issued has completed
+    if (issuer && lane == 0) mma_commit(&ms.mb_drain);
+    __syncwarp();
+  } else if (warp >= kLoaderWarp0) {
+    setmaxnreg_inc<kLoaderRegs>();
+    loader(sm, ms, tmem, w, n_tiles, warp - kLoaderWarp0, lane, a);
+  } else {
+    softmax(sm, ms, tmem, w, n_tiles, warp, lane, c_log2, a);
+  }
+
+  fence_before_sync();
+  __syncthreads();  // every TMEM read is done
+  if (warp == kWarpQK) {
+    if (lane == 0 && !mbar_wait_bounded(&ms.mb_drain, 0, kPollLimit)) record_status(a, 128);
+    __syncwarp();
     fence_after_sync();
     tmem_dealloc(tmem, kTmemCols);
-    return;
   }
-
-  // ---------------- compute warps ----------------
-  const int q = warp & 3;                  // TMEM lane quadrant
-  const int hf = warp >> 2;                // heads 32 hf .. 32 hf + 31
-  const int st = 32 * q + lane;            // softmax token
-  const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
-
-  float l_part[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
-
-  TileRegs r;
-  fetch_pages(a, w, 0, r.page_next);
-  load_tile(a, w, 0, warp, lane, st, hf, r);
-  // sigma of the tile in V'' buffer 0 / 1 (every compute thread holds the same values)
-  int sig_buf0 = dequant_tile(sm, ms, tmem, lane_base, 0, 0, r, warp, lane, hf, tid);
-  int sig_buf1 = sig_buf0;
-  if (n_tiles > 1) load_tile(a, w, 1, warp, lane, st, hf, r);
-  int sigma_prev = sig_buf0;
-
-  for (int tile = 0; tile < n_tiles; ++tile) {
-    const uint32_t par = static_cast<uint32_t>(tile & 1);
-    // ---------------- S(j): softmax of tile j ----------------
-    wait_or_abort(&ms.mb_s, par, ms, a, 1);
-    fence_after_sync();
-    float t[32];
-    {
-      uint32_t s_hi[32], s_lo[32];
-      tmem_ld32(tmem + lane_base + kColS + 32 * hf, s_hi);
-      tmem_ld32(tmem + lane_base + kColS + 64 + 32 * hf, s_lo);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(s_hi[j]) + __uint_as_float(s_lo[j]);
-      uint32_t s_pe[32];
-      tmem_ld32(tmem + lane_base + kColSpe + 32 * hf, s_pe);
-      tmem_ld_wait();
-      fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ms.mb_sfree);
-      const int sigma = par ? sig_buf1 : sig_buf0;
-      const float sig = __uint_as_float(static_cast<uint32_t>(min(max(sigma + 127, 1), 254)) << 23);
-      const bool tvalid = st < tile_valid(w, tile);
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 ac4 = *reinterpret_cast<const float4*>(&ms.ac[32 * hf + j]);
-        const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[32 * hf + j]);
-        const float acv[4] = {ac4.x, ac4.y, ac4.z, ac4.w};
-        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float base = fmaf(__uint_as_float(s_pe[j + u]), c_log2, -rv[u]);
-          t[j + u] = tvalid ? fmaf(t[j + u], acv[u] * sig, base) : -CUDART_INF_F;
-        }
-      }
-    }
-    // rescale event: first tile, a score above R + 8.5, or a new sigma
-    float tmaxv = -CUDART_INF_F;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) tmaxv = fmaxf(tmaxv, t[j]);
-    const int sigma_cur = par ? sig_buf1 : sig_buf0;
-    const bool need = compute_bar_or(tile == 0 || tmaxv > 8.5f || sigma_cur != sigma_prev);
-    if (tile > 0) {
-      // PV(j-1) must be complete before O is rescaled or P'' is overwritten
-      wait_or_abort(&ms.mb_o, par ^ 1u, ms, a, 2);
-      fence_after_sync();
-    }
-    if (need) {
-      float v[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = t[j];
-      ms.red[q][32 * hf + lane] = warp_transpose_reduce<true>(v, lane);  // tile max of x - R_old
-      named_bar(4, kCompute);
-      if (tid < kNH) {
-        const float tm = fmaxf(fmaxf(ms.red[0][tid], ms.red[1][tid]), fmaxf(ms.red[2][tid], ms.red[3][tid]));
-        // raise R so that this tile's max maps to 2^4 (only raise; the first tile sets it)
-        const float shift = tile == 0 ? tm - 4.0f : fmaxf(tm - 4.0f, 0.0f);
-        const float dshift = fmaxf(shift, -1e30f);
-        ms.R[tid] += dshift;
-        ms.beta[tid] = tile == 0 ? 1.0f : ex2(-dshift);
-        ms.alpha[tid] = tile == 0 ? 1.0f : ex2(-dshift + static_cast<float>(sigma_prev - sigma_cur));
-        ms.red[0][tid] = dshift;  // reused below as the per-head shift of t
-      }
-      named_bar(4, kCompute);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) t[j] -= ms.red[0][32 * hf + j];
-      if (tile > 0) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) l_part[j] *= ms.beta[32 * hf + j];
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * hf + cc;
-#pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t vv[32];
-            const uint32_t ta = tmem + lane_base + kColO + 64 * c + 32 * hh;
-            tmem_ld32(ta, vv);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
-            tmem_st32(ta, vv);
-          }
-        }
-        tmem_st_wait();
-      }
-    }
-    sigma_prev = sigma_cur;
-
-    // ---- P'' = exp2(t) as e4m3 hi + residual, into the MN-major B operands ----
-    {
-      uint32_t pw[8], pl[8];
-#pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        const float p0 = ex2(t[j]);
-        const float p1 = ex2(t[j + 1]);
-        l_part[j] += p0;
-        l_part[j + 1] += p1;
-        uint16_t h8, l8;
-        split_e4m3x2(p0, p1, h8, l8);
-        if ((j & 2) == 0) {
-          pw[j / 4] = h8;
-          pl[j / 4] = l8;
-        } else {
-          pw[j / 4] |= static_cast<uint32_t>(h8) << 16;
-          pl[j / 4] |= static_cast<uint32_t>(l8) << 16;
-        }
-      }
-      const int prow = (st >> 3) * kPRow + (st & 7) * 16;
-      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf) * 128) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf + 1) * 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
-      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf) * 128) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf + 1) * 128) = make_uint4(pl[4], pl[5], pl[6], pl[7]);
-    }
-    fence_proxy_async_smem();
-    fence_before_sync();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&ms.mb_pfull);
-
-    // ---------------- D(j+1): dequant the next tile into the other buffer ----------------
-    // (V'' buffer (j+1)&1 was last read by PV(j-1), complete above; its k_pe buffer by QK(j-1).)
-    if (tile + 1 < n_tiles) {
-      const int sg = dequant_tile(sm, ms, tmem, lane_base, tile + 1, sigma_cur, r, warp, lane, hf, tid);
-      if (par)
-        sig_buf0 = sg;
-      else
-        sig_buf1 = sg;
-      if (tile + 2 < n_tiles) load_tile(a, w, tile + 2, warp, lane, st, hf, r);
-    }
-  }
-
-  // ---------------- epilogue ----------------
-  wait_or_abort(&ms.mb_o, static_cast<uint32_t>((n_tiles - 1) & 1), ms, a, 4);
-  fence_after_sync();
-  {
-    const float s = warp_transpose_reduce<false>(l_part, lane);
-    ms.red[q][32 * hf + lane] = s;
-  }
-  named_bar(4, kCompute);
-  if (!ms.abort_flag) {
-    const float sig = exp2f(static_cast<float>(sigma_prev));
-    // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane
-#pragma unroll 1
-    for (int cc = 0; cc < 2; ++cc) {
-      const int c = 2 * hf + cc;
-      const int d = 128 * c + 32 * q + lane;
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t vv[32];
-        tmem_ld32(tmem + lane_base + kColO + 64 * c + 32 * hh, vv);
-        tmem_ld_wait();
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j) {
-          const int h = 32 * hh + j;
-          if (h >= w.heads_here) continue;
-          const float l = ms.red[0][h] + ms.red[1][h] + ms.red[2][h] + ms.red[3][h];
-          const float val = l > 0.f ? __uint_as_float(vv[j]) * sig / l : 0.f;
-          const int hq = w.head_base + h;
-          if (direct) {
-            a.o[w.b * a.o_stride_b + hq * a.o_stride_h + d] = __float2bfloat16_rn(val);
-          } else {
-            const int64_t row = (static_cast<int64_t>(w.b) * a.num_splits + w.split) * a.num_heads + hq;
-            a.partial_o[row * kLatent + d] = val;
-          }
-        }
-      }
-    }
-    if (!direct && tid < w.heads_here) {
-      const float l = ms.red[0][tid] + ms.red[1][tid] + ms.red[2][tid] + ms.red[3][tid];
-      const int64_t row = (static_cast<int64_t>(w.b) * a.num_splits + w.split) * a.num_heads + w.head_base + tid;
-      a.partial_lse[row] = (ms.R[tid] + __log2f(l)) * kLn2;
-    }
-  }
-  fence_before_sync();
-  named_bar(3, kThreadsTC);  // epilogue done -> warp 8 frees TMEM
 }
 
 }  // namespace

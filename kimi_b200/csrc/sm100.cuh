@@ -209,6 +209,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* mbar, uint32_t parit
   return false;
 }
 
+// As mbar_wait_bounded, but also gives up as soon as *abort (a shared-memory
+// word another thread sets when one of its own waits gave up) is non-zero.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* mbar, uint32_t parity, uint32_t max_polls,
+                                                   const volatile int* abort) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
+    if (mbar_try_wait(mbar, parity)) return true;
+    if ((i & 63u) == 63u && *abort) return false;
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// Per-warpgroup register budgets (all four warps of a warpgroup execute these)
+// ---------------------------------------------------------------------------
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
+
 // ---------------------------------------------------------------------------
 // Conversions
 // ---------------------------------------------------------------------------

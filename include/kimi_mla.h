@@ -103,22 +103,45 @@ typedef struct KimiMlaDecodeParams {
   int64_t o_stride_h;
   int32_t batch;
   int32_t num_heads;          /* 1..128 */
-  int32_t num_kv_splits;      /* 1..64, or 0 = choose from batch and SM count */
+  int32_t num_kv_splits;      /* 1..64 equal splits per sequence, or 0 = balanced schedule (below) */
   float sm_scale;
   float logit_cap;            /* must be 0 (no logit soft-capping on this path) */
 } KimiMlaDecodeParams;
 
 /* Bytes of caller-owned workspace one kimi_mla_decode call needs (split-K
- * partial outputs and log-sum-exps).  num_kv_splits as in the params (0 =
- * auto).  Returns 0 for invalid sizes. */
+ * partial outputs and log-sum-exps).  num_kv_splits as in the params.
+ * Returns 0 for invalid sizes.
+ *
+ * num_kv_splits = S > 0 cuts every sequence into S equal ranges of 128-token
+ * tiles, as the reference's num_kv_splits does (S = 1 needs no workspace).
+ * num_kv_splits = 0 selects the balanced schedule: the batch's tiles are laid
+ * end to end and split evenly over one CTA per SM per 64-head block, so ragged
+ * batches and batches smaller than the SM count keep every SM busy; sequences
+ * that one CTA covers are written directly, the others merged.  Its workspace
+ * is (batch + CTAs) x heads x 1028 bytes plus 8 bytes per sequence, rounded
+ * (partials are bf16, log-sum-exps fp32). */
 KIMI_API size_t kimi_mla_decode_workspace_size(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
 
-/* The split count kimi_mla_decode uses for these sizes (resolves 0 = auto). */
+/* S for num_kv_splits = S > 0 (capped at 64); for 0, the balanced schedule's
+ * CTAs per 64-head block on the current device. */
 KIMI_API int32_t kimi_mla_decode_num_splits(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
 
 /* Absorbed-MLA decode, one query token per sequence, one KV head. */
 KIMI_API int kimi_mla_decode(const KimiMlaDecodeParams* params, void* workspace, size_t workspace_bytes,
                     void* stream);
+
+/* The two launches of kimi_mla_decode, for callers that schedule them apart
+ * (the archive wrapper `mla_decode_mxfp4` likewise launches its stage-1
+ * kernel `_mla_decode_split_kv` and then `_mla_reduce`,
+ * archive/mla-mxfp4-dead-end/mla_decode_mxfp4_v5.py:313-376).  Same params
+ * and workspace in both calls, in stream order: kimi_mla_decode_partial runs
+ * the split-K attention (it alone writes the output when no merge is needed),
+ * kimi_mla_decode_merge the log-sum-exp merge of its partials (nothing when
+ * there are none). */
+KIMI_API int kimi_mla_decode_partial(const KimiMlaDecodeParams* params, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+KIMI_API int kimi_mla_decode_merge(const KimiMlaDecodeParams* params, void* workspace, size_t workspace_bytes,
+                                   void* stream);
 
 /* Same decode as kimi_mla_decode, for callers that cannot allocate device
  * memory.  No counterpart in the reference: aiter and the archive kernels

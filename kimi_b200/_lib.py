@@ -26,6 +26,8 @@ EXPORTED_SYMBOLS = (
     "kimi_mxfp4_kv_append",
     "kimi_mxfp4_quantize",
     "kimi_mla_decode_static_workspace",
+    "kimi_mla_decode_partial",
+    "kimi_mla_decode_merge",
 )
 
 
@@ -111,6 +113,10 @@ def load() -> ctypes.CDLL:
         lib.kimi_mla_reduce.argtypes = [ctypes.POINTER(KimiMlaReduceParams), vp]
         lib.kimi_mxfp4_kv_append.restype = ctypes.c_int
         lib.kimi_mxfp4_kv_append.argtypes = [ctypes.POINTER(KimiKvAppendParams), vp]
+        for name in ("kimi_mla_decode_partial", "kimi_mla_decode_merge"):
+            fn = getattr(lib, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [ctypes.POINTER(KimiMlaDecodeParams), vp, sz, vp]
         lib.kimi_mla_decode_static_workspace.restype = ctypes.c_int
         lib.kimi_mla_decode_static_workspace.argtypes = [ctypes.POINTER(KimiMlaDecodeParams), vp]
         lib.kimi_mxfp4_quantize.restype = ctypes.c_int

@@ -33,18 +33,6 @@ int device_sm_count() {
   return cached[dev];
 }
 
-int resolve_splits(int32_t batch, int32_t num_heads, int32_t requested) {
-  if (requested > 0) return requested > KIMI_MLA_MAX_SPLITS ? KIMI_MLA_MAX_SPLITS : requested;
-  // Auto: about one CTA per SM over (sequence, split, head block), at most 32.
-  const int head_blocks = (num_heads + 63) / 64;
-  const long ctas = static_cast<long>(batch) * head_blocks;
-  if (ctas <= 0) return 1;
-  long s = (device_sm_count() + ctas / 2) / ctas;
-  if (s < 1) s = 1;
-  if (s > 32) s = 32;
-  return static_cast<int>(s);
-}
-
 // KIMI_MLA_DECODE_KERNEL=mma selects the warp-level mma.sync decode (kept for
 // comparison); the default is the tcgen05 kernel.
 bool use_warp_mma_kernel() {
@@ -56,13 +44,52 @@ bool use_warp_mma_kernel() {
   return choice == 1;
 }
 
-size_t workspace_bytes_for(int64_t batch, int64_t heads, int64_t splits) {
-  if (splits <= 1) return 0;
-  const size_t rows = static_cast<size_t>(batch) * splits * heads;
-  size_t bytes = rows * kLatent * sizeof(float);
-  bytes = (bytes + 255) & ~static_cast<size_t>(255);
-  bytes += rows * sizeof(float);
-  return (bytes + 255) & ~static_cast<size_t>(255);
+// How one call is laid out on the GPU.
+//  * requested splits S > 0: split mode, every sequence cut into S equal tile
+//    ranges (the reference's num_kv_splits), S = 1 writing the output directly;
+//  * requested 0 (auto): balanced mode, one CTA per SM per 64-head block over
+//    the batch's tiles laid end to end (see DecodeArgs in kernels.cuh).  The
+//    mma.sync comparison kernel only has split mode; its auto choice is about
+//    one CTA per SM over (sequence, split, head block), at most 32 splits.
+struct Plan {
+  bool balanced;
+  int ctas;  // balanced: CTAs per head block; split mode: splits per sequence
+};
+
+Plan resolve_plan(int32_t batch, int32_t num_heads, int32_t requested) {
+  const int head_blocks = (num_heads + 63) / 64;
+  if (requested > 0) return {false, requested > KIMI_MLA_MAX_SPLITS ? KIMI_MLA_MAX_SPLITS : requested};
+  if (!use_warp_mma_kernel()) {
+    const int c = device_sm_count() / head_blocks;
+    return {true, c < 1 ? 1 : c};
+  }
+  const long ctas = static_cast<long>(batch) * head_blocks;
+  if (ctas <= 0) return {false, 1};
+  long s = (device_sm_count() + ctas / 2) / ctas;
+  if (s < 1) s = 1;
+  if (s > 32) s = 32;
+  return {false, static_cast<int>(s)};
+}
+
+inline size_t round256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+// Workspace: partial outputs [slots, heads, 512] bf16 (each normalised by its own
+// softmax sum, so bf16 costs one rounding like the output's), log-sum-exps [slots,
+// heads] fp32, then (balanced mode) [batch] int2 CTA spans.  Split mode has
+// batch * S slots (none for S = 1), balanced mode batch + ctas.
+struct Layout {
+  size_t slots, po_bytes, lse_bytes, meta_bytes;
+  size_t total() const { return po_bytes + lse_bytes + meta_bytes; }
+};
+
+Layout workspace_layout(int64_t batch, int64_t heads, const Plan& plan) {
+  Layout l{};
+  if (!plan.balanced && plan.ctas <= 1) return l;
+  l.slots = plan.balanced ? static_cast<size_t>(batch + plan.ctas) : static_cast<size_t>(batch) * plan.ctas;
+  l.po_bytes = round256(l.slots * heads * kLatent * sizeof(__nv_bfloat16));
+  l.lse_bytes = round256(l.slots * heads * sizeof(float));
+  l.meta_bytes = plan.balanced ? round256(static_cast<size_t>(batch) * 2 * sizeof(int32_t)) : 0;
+  return l;
 }
 
 }  // namespace
@@ -90,15 +117,25 @@ const char* kimi_status_string(int status) {
 
 int32_t kimi_mla_decode_num_splits(int32_t batch, int32_t num_heads, int32_t num_kv_splits) {
   if (batch < 0 || num_heads < 1 || num_heads > KIMI_MLA_MAX_HEADS || num_kv_splits < 0) return 0;
-  return resolve_splits(batch, num_heads, num_kv_splits);
+  return resolve_plan(batch, num_heads, num_kv_splits).ctas;
 }
 
 size_t kimi_mla_decode_workspace_size(int32_t batch, int32_t num_heads, int32_t num_kv_splits) {
   if (batch < 0 || num_heads < 1 || num_heads > KIMI_MLA_MAX_HEADS || num_kv_splits < 0) return 0;
-  return workspace_bytes_for(batch, num_heads, resolve_splits(batch, num_heads, num_kv_splits));
+  return workspace_layout(batch, num_heads, resolve_plan(batch, num_heads, num_kv_splits)).total();
 }
 
-int kimi_mla_decode(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Checked arguments of one decode call, ready to launch.
+struct Prepared {
+  Plan plan;
+  kimi::DecodeArgs args;
+};
+
+int prepare(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, Prepared& out) {
   if (!p) return KIMI_ERR_NULL_POINTER;
   if (p->batch < 0 || p->num_heads < 1 || p->num_heads > KIMI_MLA_MAX_HEADS || p->num_kv_splits < 0 ||
       p->num_kv_splits > KIMI_MLA_MAX_SPLITS || p->num_pages < 0)
@@ -112,16 +149,15 @@ int kimi_mla_decode(const KimiMlaDecodeParams* p, void* workspace, size_t worksp
     return KIMI_ERR_BAD_STRIDE;
   if (!aligned(p->q, 16) || !aligned(p->kv_buffer, 16) || !aligned(p->kv_scales, 16) || !aligned(p->o, 8))
     return KIMI_ERR_MISALIGNED;
-  const int splits = resolve_splits(p->batch, p->num_heads, p->num_kv_splits);
-  const size_t need = workspace_bytes_for(p->batch, p->num_heads, splits);
+  const Plan plan = resolve_plan(p->batch, p->num_heads, p->num_kv_splits);
+  const Layout lay = workspace_layout(p->batch, p->num_heads, plan);
+  const size_t need = lay.total();
   if (need > 0) {
     if (!workspace || workspace_bytes < need) return KIMI_ERR_WORKSPACE_TOO_SMALL;
     if (!aligned(workspace, 256)) return KIMI_ERR_MISALIGNED;
   }
-  const size_t rows = static_cast<size_t>(p->batch) * splits * p->num_heads;
-  const size_t po_bytes = (rows * kLatent * sizeof(float) + 255) & ~static_cast<size_t>(255);
-
-  kimi::DecodeArgs a;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  kimi::DecodeArgs& a = out.args;
   a.q = static_cast<const __nv_bfloat16*>(p->q);
   a.q_stride_b = p->q_stride_b;
   a.q_stride_h = p->q_stride_h;
@@ -134,27 +170,66 @@ int kimi_mla_decode(const KimiMlaDecodeParams* p, void* workspace, size_t worksp
   a.o = static_cast<__nv_bfloat16*>(p->o);
   a.o_stride_b = p->o_stride_b;
   a.o_stride_h = p->o_stride_h;
-  a.partial_o = need ? static_cast<float*>(workspace) : nullptr;
-  a.partial_lse = need ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + po_bytes) : nullptr;
+  a.partial_o = need ? reinterpret_cast<__nv_bfloat16*>(ws) : nullptr;
+  a.partial_lse = need ? reinterpret_cast<float*>(ws + lay.po_bytes) : nullptr;
+  a.seq_meta = plan.balanced ? reinterpret_cast<int2*>(ws + lay.po_bytes + lay.lse_bytes) : nullptr;
   a.batch = p->batch;
   a.num_heads = p->num_heads;
-  a.num_splits = splits;
+  a.num_splits = plan.ctas;
+  a.balanced = plan.balanced ? 1 : 0;
   a.sm_scale = p->sm_scale;
   a.status = nullptr;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = use_warp_mma_kernel() ? kimi::launch_decode_mma(a, s) : kimi::launch_decode_tc(a, s);
-  if (e != cudaSuccess || splits == 1) return cuda_status(e);
+  out.plan = plan;
+  return KIMI_OK;
+}
 
+int launch_stage1(const Prepared& pr, cudaStream_t s) {
+  return cuda_status(use_warp_mma_kernel() ? kimi::launch_decode_mma(pr.args, s) : kimi::launch_decode_tc(pr.args, s));
+}
+
+int launch_merge(const Prepared& pr, cudaStream_t s) {
+  if (!pr.plan.balanced && pr.plan.ctas == 1) return KIMI_OK;  // stage 1 wrote the output
+  const kimi::DecodeArgs& a = pr.args;
   kimi::ReduceArgs r;
   r.partial_o = a.partial_o;
+  r.partial_bf16 = 1;
   r.partial_lse = a.partial_lse;
   r.o = a.o;
   r.o_stride_b = a.o_stride_b;
   r.o_stride_h = a.o_stride_h;
   r.batch = a.batch;
   r.num_heads = a.num_heads;
-  r.num_splits = splits;
+  r.num_splits = pr.plan.ctas;
+  r.seq_meta = a.seq_meta;
+  r.kv_indptr = a.kv_indptr;
   return cuda_status(kimi::launch_reduce(r, s));
+}
+
+}  // namespace
+
+extern "C" {
+
+int kimi_mla_decode(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, void* stream) {
+  Prepared pr;
+  int st = prepare(p, workspace, workspace_bytes, pr);
+  if (st != KIMI_OK || p->batch == 0) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = launch_stage1(pr, s);
+  return st != KIMI_OK ? st : launch_merge(pr, s);
+}
+
+int kimi_mla_decode_partial(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, void* stream) {
+  Prepared pr;
+  const int st = prepare(p, workspace, workspace_bytes, pr);
+  if (st != KIMI_OK || p->batch == 0) return st;
+  return launch_stage1(pr, static_cast<cudaStream_t>(stream));
+}
+
+int kimi_mla_decode_merge(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, void* stream) {
+  Prepared pr;
+  const int st = prepare(p, workspace, workspace_bytes, pr);
+  if (st != KIMI_OK || p->batch == 0) return st;
+  return launch_merge(pr, static_cast<cudaStream_t>(stream));
 }
 
 int kimi_mla_reduce(const KimiMlaReduceParams* p, void* stream) {
@@ -168,6 +243,7 @@ int kimi_mla_reduce(const KimiMlaReduceParams* p, void* stream) {
   if (!aligned(p->partial_o, 16) || !aligned(p->partial_lse, 4) || !aligned(p->o, 8)) return KIMI_ERR_MISALIGNED;
   kimi::ReduceArgs r;
   r.partial_o = p->partial_o;
+  r.partial_bf16 = 0;
   r.partial_lse = p->partial_lse;
   r.o = static_cast<__nv_bfloat16*>(p->o);
   r.o_stride_b = p->o_stride_b;
@@ -175,6 +251,8 @@ int kimi_mla_reduce(const KimiMlaReduceParams* p, void* stream) {
   r.batch = p->batch;
   r.num_heads = p->num_heads;
   r.num_splits = p->num_splits;
+  r.seq_meta = nullptr;
+  r.kv_indptr = nullptr;
   return cuda_status(kimi::launch_reduce(r, static_cast<cudaStream_t>(stream)));
 }
 

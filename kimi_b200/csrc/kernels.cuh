@@ -43,9 +43,18 @@ struct QuantizeArgs {
   int legacy_rule;
 };
 
-// Split-K decode: stage 1 writes per-(sequence, split, head) partial outputs
-// normalised by the split's own softmax sum plus the natural-log
-// log-sum-exp; with one split it writes the final bf16 output directly.
+// Split-K decode.  Stage 1 covers each sequence's 128-token tiles with one or
+// more pieces; a piece that holds a whole sequence writes the final bf16
+// output, any other writes a partial output (normalised by its own softmax
+// sum) and its natural-log log-sum-exp to a workspace slot.
+//   * split mode (balanced = 0): grid (num_splits, batch, head blocks); CTA
+//     (s, b) takes the s-th of num_splits equal tile ranges of sequence b, slot
+//     b * num_splits + s; with one split the CTA writes the output directly.
+//   * balanced mode (balanced = 1): grid (ctas, 1, head blocks); CTA c takes
+//     tiles [c T / ctas, (c + 1) T / ctas) of all T tiles of the batch laid end
+//     to end, slot b + c for its piece of sequence b (unique: along the tile
+//     list both b and c only grow), and the CTA holding a sequence's first tile
+//     records (first CTA, last CTA) of that sequence in seq_meta for the merge.
 struct DecodeArgs {
   const __nv_bfloat16* q;
   int64_t q_stride_b;
@@ -59,24 +68,29 @@ struct DecodeArgs {
   __nv_bfloat16* o;
   int64_t o_stride_b;
   int64_t o_stride_h;
-  float* partial_o;    // [batch, splits, heads, 512]
+  __nv_bfloat16* partial_o;  // [slots, heads, 512] bf16 (the merge restores fp32 sums)
   float* partial_lse;  // [batch, splits, heads]
   int* status;         // optional device word: bits set when a bounded wait gave up
+  int2* seq_meta;      // balanced mode: [batch] (first CTA, last CTA) of each sequence's tiles
   int batch;
   int num_heads;
-  int num_splits;
+  int num_splits;      // split mode: splits per sequence
+  int balanced;        // 1: balanced mode (gridDim.x CTAs per head block)
   float sm_scale;
 };
 
 struct ReduceArgs {
-  const float* partial_o;
+  const void* partial_o;      // [slots, heads, 512], bf16 (this library's decode) or fp32
+  int partial_bf16;
   const float* partial_lse;
   __nv_bfloat16* o;
   int64_t o_stride_b;
   int64_t o_stride_h;
   int batch;
   int num_heads;
-  int num_splits;
+  int num_splits;             // split mode: slots b * num_splits + s
+  const int2* seq_meta;       // balanced mode (non-null): slots b + c, c in [meta.x, meta.y]
+  const int32_t* kv_indptr;   // balanced mode: sequences without pages get zeros
 };
 
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);

@@ -334,11 +334,11 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_mma_kernel(DecodeArgs 
             pack_bf16x2(o_acc[j][2 * r] * inv_l[r], o_acc[j][2 * r + 1] * inv_l[r]);
     } else {
       const int64_t row = (static_cast<int64_t>(b) * a.num_splits + split) * a.num_heads + hq;
-      float* prow = a.partial_o + row * kLatent + half * 256 + cq;
+      __nv_bfloat16* prow = a.partial_o + row * kLatent + half * 256 + cq;
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        *reinterpret_cast<float2*>(prow + j * 8) =
-            make_float2(o_acc[j][2 * r] * inv_l[r], o_acc[j][2 * r + 1] * inv_l[r]);
+        *reinterpret_cast<uint32_t*>(prow + j * 8) =
+            pack_bf16x2(o_acc[j][2 * r] * inv_l[r], o_acc[j][2 * r + 1] * inv_l[r]);
       if (half == 0 && (lane & 3) == 0) a.partial_lse[row] = lse[r];
     }
   }

@@ -6,7 +6,12 @@
 // with the contract of `reference_mla_decode` (tests/test_triton_mla_decode.py:12-62):
 //   S = q_nope . k_nope + q_pe . k_pe,  P = softmax(S * sm_scale),  O = P . k_nope.
 //
-// One CTA = a sequence, a range of its pages, up to 64 heads.
+// One CTA = up to 64 heads over a run of 128-token tiles: a range of one
+// sequence (split mode) or a range of the whole batch's tiles laid end to end,
+// which may cross sequence boundaries (balanced mode; see DecodeArgs).  The
+// roles walk that run with identical cursors; at a sequence boundary the
+// softmax warps finish the piece (its output or partial) and build the next
+// sequence's Q'' before the QK issuer continues.
 //   * The cache is consumed in tiles of 128 tokens (two pages).  Tokens sit on
 //     the MMA's M dimension (M = 128) and heads on N ("swap AB").
 //   * Each latent element is dequantised ONCE per tile into an 8-bit tile V''
@@ -73,7 +78,7 @@ constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr int kLoaderThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColSpe = 128, kColKpe = 192, kColO = 256;
-constexpr uint32_t kPollLimit = 1u << 22;
+constexpr uint32_t kPollLimit = 100000;  // polls of up to kWaitSleepNs each: about 2 s
 // Register budgets: 512 threads launch with 128 registers each (65536).  The
 // loader warpgroup takes 184, the issuer warpgroup gives back down to 72:
 // 256 * 128 + 128 * 184 + 128 * 72 = 65536.
@@ -84,6 +89,7 @@ static_assert(256 * 128 + 128 * kLoaderRegs + 128 * kIssuerRegs <= kThreadsTC * 
 // Named barriers (0 is __syncthreads)
 constexpr int kBarSoftmax = 1;
 constexpr int kBarLoader = 2;
+constexpr int kBarSetup = 3;  // all 512 threads, once: barriers, TMEM and the first Q'' are ready
 
 // Shared memory (bytes).  Core matrix (r, c) of an operand lives at
 // r * row_stride + c * 128, 16 bytes per row inside the core.
@@ -109,6 +115,12 @@ struct Misc {
   uint64_t mb_sfree;      // S(j) read out of TMEM (8 softmax warp arrivals)
   uint64_t mb_pfull;      // P''(j) written, O rescaled (8 softmax warp arrivals)
   uint64_t mb_drain;      // each issuer's last commit (1 + kPvIssuers arrivals)
+  uint64_t mb_qready;     // Q'' of the next piece's sequence written (8 softmax warp arrivals)
+  long long sched_pos0;   // balanced mode: global position of the CTA's first tile
+  long long sched_total;  // balanced mode: tiles of the whole batch
+  int sched_b0, sched_off0, sched_count;
+  int sched_tmin, sched_tmax;
+  int scan_warp[16];      // block scan scratch
   uint32_t tmem_base;
   int abort_flag;
   int tile_smax[4];       // max e8m0 byte of tile j in slot j % 4 (reset two tiles ahead)
@@ -123,7 +135,7 @@ constexpr int kSmemTC = kOffMisc + static_cast<int>(sizeof(Misc));
 static_assert(kSmemTC <= 232448, "shared memory budget");
 static_assert(kOffMisc % 16 == 0 && offsetof(Misc, ac) % 16 == 0 && offsetof(Misc, R) % 16 == 0,
               "per-head arrays are read with 16-byte vector loads");
-static_assert(offsetof(Misc, mb_vfull) % 8 == 0 && offsetof(Misc, mb_drain) % 8 == 0, "mbarriers are 8-byte aligned");
+static_assert(offsetof(Misc, mb_vfull) % 8 == 0 && offsetof(Misc, mb_qready) % 8 == 0, "mbarriers are 8-byte aligned");
 
 __device__ __forceinline__ uint8_t* smem_base() {
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
@@ -132,6 +144,13 @@ __device__ __forceinline__ uint8_t* smem_base() {
 
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+// End of setup, reached by every role from its own code path.
+__device__ __forceinline__ void setup_barrier() {
+  fence_before_sync();
+  named_bar(kBarSetup, kThreadsTC);
+  fence_after_sync();
 }
 
 // Barrier over `count` threads that also ORs a predicate across them.
@@ -261,15 +280,162 @@ __device__ __forceinline__ void split_e4m3x2(float p0, float p1, uint16_t& hi, u
   lo = l8;
 }
 
-struct WorkItem {
-  int b, split, head_base, heads_here;
-  int page_lo, n_pages, n_tok, p_begin, p_end;
+// ---------------------------------------------------------------------------
+// Tile schedule and cursors
+// ---------------------------------------------------------------------------
+// A CTA's run of tiles: `count` tiles starting at tile off0 of sequence b0
+// (global position pos0 of the batch's tile list in balanced mode).
+struct Sched {
+  int b0, off0, count;
+  long long pos0, total;
+  // balanced mode with every sequence `seq_tiles` long and batch <= CTAs: each
+  // sequence gets `per_seq` equal splits of `split_tiles` tiles (CTA b * per_seq
+  // + s takes split s of sequence b), so no CTA straddles two sequences
+  int per_seq, split_tiles, seq_tiles;
 };
 
-// Number of this split's tokens in tile j (arithmetic only).
-__device__ __forceinline__ int tile_valid(const WorkItem& w, int tile) {
-  const int p0 = w.p_begin + 2 * tile;
-  return max(0, min(min(kPageSize * 2, w.n_tok - p0 * kPageSize), (w.p_end - p0) * kPageSize));
+// Position in the run.  A piece is the part of one sequence inside the run:
+// tiles [piece_begin, piece_end) of sequence b; `left` tiles of the run follow it.
+struct Cursor {
+  int b, tile, piece_begin, piece_end, left;
+  int page_lo, n_pages, n_tok;
+  long long seq_pos;  // global position of tile 0 of sequence b (balanced mode)
+};
+
+__device__ __forceinline__ int seq_tiles_of(const DecodeArgs& a, int b) {
+  const int n = a.kv_indptr[b + 1] - a.kv_indptr[b];
+  return n > 0 ? (n + 1) >> 1 : 0;
+}
+
+__device__ __forceinline__ int cursor_tiles(const Cursor& c) { return (c.n_pages + 1) >> 1; }
+
+__device__ __forceinline__ void cursor_load_seq(const DecodeArgs& a, Cursor& c) {
+  c.page_lo = a.kv_indptr[c.b];
+  c.n_pages = max(a.kv_indptr[c.b + 1] - c.page_lo, 0);
+  const int last =
+      c.n_pages == 0 ? 0 : min(max(a.kv_last_page_len ? a.kv_last_page_len[c.b] : kPageSize, 1), kPageSize);
+  c.n_tok = c.n_pages == 0 ? 0 : (c.n_pages - 1) * kPageSize + last;
+}
+
+__device__ __forceinline__ void cursor_start(const DecodeArgs& a, const Sched& s, Cursor& c) {
+  c.b = s.b0;
+  cursor_load_seq(a, c);
+  c.tile = c.piece_begin = s.off0;
+  c.piece_end = min(cursor_tiles(c), s.off0 + s.count);
+  c.left = s.count - (c.piece_end - s.off0);
+  c.seq_pos = s.pos0 - s.off0;
+}
+
+// Step to the next tile of the run (past its end the cursor stays in the last piece).
+__device__ __forceinline__ void cursor_next(const DecodeArgs& a, Cursor& c) {
+  if (++c.tile < c.piece_end || c.left <= 0) return;
+  c.seq_pos += cursor_tiles(c);
+  do {
+    ++c.b;
+    cursor_load_seq(a, c);
+  } while (cursor_tiles(c) == 0 && c.b + 1 < a.batch);
+  c.tile = c.piece_begin = 0;
+  c.piece_end = min(cursor_tiles(c), c.left);
+  c.left -= c.piece_end;
+}
+
+__device__ __forceinline__ bool cursor_first(const Cursor& c) { return c.tile == c.piece_begin; }
+__device__ __forceinline__ bool cursor_last(const Cursor& c) { return c.tile + 1 == c.piece_end; }
+__device__ __forceinline__ int cursor_valid(const Cursor& c) {
+  return max(0, min(kPageSize * 2, c.n_tok - c.tile * kPageSize * 2));
+}
+
+// CTA of a global tile position in balanced mode: aligned splits (see Sched),
+// else the largest c with c T / G <= x.
+__device__ __forceinline__ int cta_of_tile(long long x, const Sched& s, int ctas) {
+  if (s.per_seq > 0) {
+    const long long b = x / s.seq_tiles;
+    return static_cast<int>(b * s.per_seq + (x - b * s.seq_tiles) / s.split_tiles);
+  }
+  return static_cast<int>(((x + 1) * ctas - 1) / s.total);
+}
+
+// Balanced mode: locate this CTA's run with a block-wide scan of the tiles per
+// sequence (all threads of the CTA call this).
+__device__ void balanced_schedule(const DecodeArgs& a, Misc& ms, Sched& s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    ms.sched_tmin = 0x7fffffff;
+    ms.sched_tmax = 0;
+  }
+  __syncthreads();
+  const int per = (a.batch + kThreadsTC - 1) / kThreadsTC;
+  const int lo = min(a.batch, tid * per), hi = min(a.batch, lo + per);
+  int mine = 0, tmin = 0x7fffffff, tmax = 0;
+  for (int b = lo; b < hi; ++b) {
+    const int t = seq_tiles_of(a, b);
+    mine += t;
+    tmin = min(tmin, t);
+    tmax = max(tmax, t);
+  }
+  tmin = __reduce_min_sync(0xffffffffu, static_cast<unsigned>(tmin));
+  tmax = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(tmax));
+  if (lane == 0) {
+    atomicMin(&ms.sched_tmin, tmin);
+    atomicMax(&ms.sched_tmax, tmax);
+  }
+  int incl = mine;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += v;
+  }
+  if (lane == 31) ms.scan_warp[warp] = incl;
+  __syncthreads();
+  int before = 0, total = 0;
+  for (int w2 = 0; w2 < kThreadsTC / 32; ++w2) {
+    const int v = ms.scan_warp[w2];
+    if (w2 < warp) before += v;
+    total += v;
+  }
+  const int excl = before + incl - mine;
+  const int ctas = gridDim.x, c = blockIdx.x;
+  long long start = static_cast<long long>(c) * total / ctas;
+  long long end = static_cast<long long>(c + 1) * total / ctas;
+  const int seq_t = ms.sched_tmax;
+  s.per_seq = (ms.sched_tmin == seq_t && seq_t > 0 && a.batch <= ctas) ? ctas / a.batch : 0;
+  s.seq_tiles = seq_t;
+  s.split_tiles = s.per_seq > 0 ? (seq_t + s.per_seq - 1) / s.per_seq : 0;
+  if (s.per_seq > 0) {
+    // uniform batch: whole-sequence splits (CTAs past batch * per_seq stay idle)
+    const int b = c / s.per_seq, split = c % s.per_seq;
+    start = end = total;
+    if (b < a.batch) {
+      const int off = min(split * s.split_tiles, seq_t);
+      start = static_cast<long long>(b) * seq_t + off;
+      end = static_cast<long long>(b) * seq_t + min(off + s.split_tiles, seq_t);
+    }
+  }
+  // (also for an empty run: the sequence at its position names its merge slot)
+  if (start < total && excl <= start && start < excl + mine) {
+    long long acc = excl;
+    for (int b = lo; b < hi; ++b) {
+      const int t = seq_tiles_of(a, b);
+      if (start < acc + t) {
+        ms.sched_b0 = b;
+        ms.sched_off0 = static_cast<int>(start - acc);
+        break;
+      }
+      acc += t;
+    }
+  }
+  if (tid == 0) {
+    ms.sched_count = static_cast<int>(end - start);
+    ms.sched_pos0 = (s.per_seq > 0 && end == start) ? total : start;  // idle aligned CTAs own no slot
+    ms.sched_total = total;
+  }
+  __syncthreads();
+  s.count = ms.sched_count;
+  s.b0 = ms.sched_pos0 < total ? ms.sched_b0 : 0;
+  s.off0 = ms.sched_pos0 < total ? ms.sched_off0 : 0;
+  s.pos0 = ms.sched_pos0;
+  s.total = ms.sched_total;
+  __syncthreads();  // the scan scratch is reused
 }
 
 // Raw data of one tile held by one loader thread (quadrant q = its warp - 8,
@@ -286,6 +452,7 @@ struct RawTile {
   uint32_t sb[16];
   uint4 pe[8];
   int nvalid;
+  bool first;        // first tile of a piece
   int page_next[2];  // page ids of the tile loaded next (fetched one tile ahead)
   int page_pf[2];    // page ids of the tile prefetched into L2 next (loader thread 0 only)
 };
@@ -294,19 +461,21 @@ struct RawTile {
 // in L2, fetched while tiles j - kPrefetchTiles .. j - 1 were processed.
 constexpr int kPrefetchTiles = 3;
 
-__device__ __forceinline__ void fetch_pages(const DecodeArgs& a, const WorkItem& w, int tile, int (&pg)[2]) {
+__device__ __forceinline__ void fetch_pages(const DecodeArgs& a, const Cursor& c, int (&pg)[2]) {
 #pragma unroll
   for (int slot = 0; slot < 2; ++slot) {
-    const int p = w.p_begin + 2 * tile + slot;
-    const bool in_range = p < w.p_end;
-    pg[slot] = ldg_s32_or(a.kv_indices + w.page_lo + (in_range ? p : 0), in_range, -1);
+    const int p = 2 * c.tile + slot;
+    const bool in_range = p < c.n_pages;
+    pg[slot] = ldg_s32_or(a.kv_indices + c.page_lo + (in_range ? p : 0), in_range, -1);
   }
 }
 
-__device__ __forceinline__ void load_tile(const DecodeArgs& a, const WorkItem& w, int tile, int q, int lane,
+// Registers of tile `c` (page ids already in r.page_next); then the page ids of tile `next`.
+__device__ __forceinline__ void load_tile(const DecodeArgs& a, const Cursor& c, const Cursor& next, int q, int lane,
                                           RawTile& r) {
-  const int nvalid = tile_valid(w, tile);
+  const int nvalid = cursor_valid(c);
   r.nvalid = nvalid;
+  r.first = cursor_first(c);
   const int pid = (q >> 1) ? r.page_next[1] : r.page_next[0];  // (a select keeps page_next in registers)
   const int page = (pid >= 0 && pid < a.num_pages) ? pid : -1;
   const uint8_t* pbase = a.kv_buffer + static_cast<int64_t>(page < 0 ? 0 : page) * kPageBytes;
@@ -327,9 +496,10 @@ __device__ __forceinline__ void load_tile(const DecodeArgs& a, const WorkItem& w
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int tk = 32 * q + 4 * k + (lane >> 3);
-    r.pe[k] = ldg_stream_if(pbase + (tk & 63) * kTokenBytes + kNibbleBytes + 16 * (lane & 7), page >= 0 && tk < nvalid);
+    r.pe[k] = ldg_stream_if(pbase + (tk & 63) * kTokenBytes + kNibbleBytes + 16 * (lane & 7),
+                            page >= 0 && tk < nvalid);
   }
-  fetch_pages(a, w, tile + 1, r.page_next);
+  fetch_pages(a, next, r.page_next);
 }
 
 // Loader thread 0: prefetch the pages (cache rows and scales) of one tile into L2.
@@ -340,6 +510,17 @@ __device__ __forceinline__ void prefetch_tile(const DecodeArgs& a, const int (&p
       prefetch_l2(a.kv_buffer + static_cast<int64_t>(pg[slot]) * kPageBytes, kPageBytes);
       prefetch_l2(a.kv_scales + static_cast<int64_t>(pg[slot]) * kPageScaleBytes, kPageScaleBytes);
     }
+  }
+}
+
+// Prefetch the q rows of sequence b (this CTA's heads) into L2; thread `i` of
+// `n` cooperating threads issues its share.
+__device__ __forceinline__ void prefetch_q(const DecodeArgs& a, int b, int head_base, int heads_here, int i, int n) {
+  const __nv_bfloat16* base = a.q + static_cast<int64_t>(b) * a.q_stride_b + static_cast<int64_t>(head_base) * a.q_stride_h;
+  if (a.q_stride_h == kQkDim) {
+    if (i == 0) prefetch_l2(base, static_cast<uint32_t>(heads_here * kQkDim * 2));
+  } else {
+    for (int h = i; h < heads_here; h += n) prefetch_l2(base + static_cast<int64_t>(h) * a.q_stride_h, kQkDim * 2);
   }
 }
 
@@ -383,14 +564,22 @@ __device__ __forceinline__ bool warp_wait(uint64_t* mb, uint32_t parity, Misc& m
 // ---------------------------------------------------------------------------
 // Issuers (warps 12..15; lane 0 issues)
 // ---------------------------------------------------------------------------
-__device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int lane, const DecodeArgs& a) {
+__device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int lane, const DecodeArgs& a) {
   const uint32_t id_qk = instr_desc(kFmtE5M2, kFmtE4M3, false, false, 128, 128);
   const uint32_t id_pe = instr_desc(kFmtBF16, kFmtBF16, false, false, 128, 64);
   const uint32_t sQ = smem_addr(sm + kOffQ), sQpe = smem_addr(sm + kOffQpe);
-  for (int j = 0; j < n_tiles; ++j) {
-    // QK(j) needs V''(j)/k_pe(j) written and S(j-1) read out of TMEM (single S buffer)
+  Cursor cur;
+  cursor_start(a, sc, cur);
+  int pieces = 0;
+  for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
+    // QK(j) needs V''(j)/k_pe(j) written and S(j-1) read out of TMEM (single S
+    // buffer); the first tile of a later piece also needs that sequence's Q''.
     if (!warp_wait(&ms.mb_vfull[j & 1], static_cast<uint32_t>((j >> 1) & 1), ms, a, 16, lane)) break;
     if (j > 0 && !warp_wait(&ms.mb_sfree, static_cast<uint32_t>((j - 1) & 1), ms, a, 16, lane)) break;
+    if (j > 0 && cursor_first(cur)) {
+      if (!warp_wait(&ms.mb_qready, static_cast<uint32_t>(pieces & 1), ms, a, 16, lane)) break;
+      ++pieces;
+    }
     fence_after_sync();
     if (lane == 0) {
       const uint32_t sV = smem_addr(sm + kOffV + (j & 1) * kVBytes);
@@ -411,24 +600,29 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int
 }
 
 // PV issuer p owns latent chunks 2p and 2p + 1.
-__device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int lane, int p, const DecodeArgs& a) {
+__device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int lane, int p,
+                          const DecodeArgs& a) {
   const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, 64);
   const uint32_t sP = smem_addr(sm + kOffP), sPlo = smem_addr(sm + kOffPlo);
   const int c0 = 2 * p;
   const int c1 = 2 * p + 2;
-  for (int j = 0; j < n_tiles; ++j) {
-    // PV(j) needs P''(j) (written after PV(j-1) completed and O was rescaled)
+  Cursor cur;
+  cursor_start(a, sc, cur);
+  for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
+    // PV(j) needs P''(j) (written after PV(j-1) completed and O was rescaled or,
+    // at a piece start, read out by the previous piece's epilogue)
     if (!warp_wait(&ms.mb_pfull, static_cast<uint32_t>(j & 1), ms, a, 32, lane)) break;
     fence_after_sync();
     if (lane == 0) {
       const uint32_t sV = smem_addr(sm + kOffV + (j & 1) * kVBytes);
+      const bool fresh = cursor_first(cur);  // the piece's first PV starts the accumulator
 #pragma unroll 1
       for (int k = 0; k < 4; ++k) {
         const uint64_t phi = smem_desc(sP + k * 4 * kPRow, kPRow, 128);
         const uint64_t plo = smem_desc(sPlo + k * 4 * kPRow, kPRow, 128);
         for (int c = c0; c < c1; ++c)
           mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B), phi,
-                        id_pv, (j > 0 || k > 0) ? 1u : 0u);
+                        id_pv, (fresh && k == 0) ? 0u : 1u);
         for (int c = c0; c < c1; ++c)
           mma_f8f6f4_ss(tmem + kColO + 64 * c, smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B), plo,
                         id_pv, 1u);
@@ -442,24 +636,42 @@ __device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, int n_tiles, int
 // ---------------------------------------------------------------------------
 // Loaders (warps 8..11): V''(j) and k_pe(j) from registers, then the next tile's loads
 // ---------------------------------------------------------------------------
-__device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w, int n_tiles, int q, int lane,
+__device__ void loader(uint8_t* sm, Misc& ms, const Sched& sc, int head_base, int heads_here, int q, int lane,
                        const DecodeArgs& a) {
   const int ltid = 32 * q + lane;
   const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
   const int e = (lane >> 2) & 1, g = (lane & 3) | ((lane >> 3) << 2);
+  // lc: the tile whose registers are loaded; fc: the next one (its page ids are
+  // fetched one tile ahead); pc: the tile loader thread 0 last prefetched into L2.
+  Cursor lc, fc;
+  cursor_start(a, sc, lc);
+  fc = lc;
+  cursor_next(a, fc);
   RawTile r;
-  fetch_pages(a, w, 0, r.page_next);
-  if (ltid == 0) {
-    // tiles 1 .. kPrefetchTiles now; tile j + kPrefetchTiles when tile j is loaded
-    for (int t = 1; t <= kPrefetchTiles; ++t) {
-      fetch_pages(a, w, t, r.page_pf);
-      prefetch_tile(a, r.page_pf);
+  fetch_pages(a, lc, r.page_next);
+  // page ids of tiles 1 .. kPrefetchTiles, requested together with tile 0's
+  Cursor pc = lc;
+  int pf_ids[kPrefetchTiles][2];
+#pragma unroll
+  for (int t = 0; t < kPrefetchTiles; ++t) {
+    cursor_next(a, pc);
+    if (ltid == 0 && t + 1 < sc.count) {
+      fetch_pages(a, pc, pf_ids[t]);
+    } else {
+      pf_ids[t][0] = pf_ids[t][1] = -1;
     }
-    fetch_pages(a, w, kPrefetchTiles + 1, r.page_pf);
   }
-  load_tile(a, w, 0, q, lane, r);
+  // the first tile's loads overlap the setup (TMEM, barriers, Q''), then the
+  // next tiles are prefetched into L2
+  load_tile(a, lc, fc, q, lane, r);
+  if (ltid == 0) {
+#pragma unroll
+    for (int t = 0; t < kPrefetchTiles; ++t) prefetch_tile(a, pf_ids[t]);
+  }
+  setup_barrier();
+  const uint32_t tmem = ms.tmem_base;
   int prev_sigma = 0;
-  for (int j = 0; j < n_tiles; ++j) {
+  for (int j = 0; j < sc.count; ++j) {
     const int buf = j & 1;
     // V'' buffer j & 1 (and its k_pe TMEM buffer) was last read by PV(j-2) / QK(j-2)
     bool ok = true;
@@ -473,7 +685,7 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w, 
     if (bar_or(kBarLoader, kLoaderThreads, !ok)) break;
     const int smax = ms.tile_smax[j & 3];
     int sigma;
-    if (j == 0) {
+    if (r.first) {
       sigma = smax - 127 - 8;  // tile max maps to <= 6 * 2^8 in V''
     } else {
       const int kmax = smax - 127 - prev_sigma;
@@ -528,36 +740,133 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w, 
     fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(&ms.mb_vfull[buf]);
-    if (j + 1 < n_tiles) {
-      if (ltid == 0) {
-        prefetch_tile(a, r.page_pf);  // tile j + 1 + kPrefetchTiles (ids fetched one tile ago)
-        fetch_pages(a, w, j + 2 + kPrefetchTiles, r.page_pf);
+    if (j + 1 < sc.count) {
+      lc = fc;
+      cursor_next(a, fc);
+      if (ltid == 0 && j + 1 + kPrefetchTiles < sc.count) {
+        cursor_next(a, pc);  // tile j + 1 + kPrefetchTiles
+        fetch_pages(a, pc, r.page_pf);
+        prefetch_tile(a, r.page_pf);
+        // a new sequence ahead: its q rows, for the softmax warps' Q'' rebuild
+        if (cursor_first(pc)) prefetch_q(a, pc.b, head_base, heads_here, 0, 1);
       }
-      load_tile(a, w, j + 1, q, lane, r);
+      load_tile(a, lc, fc, q, lane, r);
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// Softmax warps (0..7) and the epilogue
+// Q'' of one sequence (softmax threads 0..255: 4 per head; part p handles latent
+// [128p, 128p + 128) and RoPE [16p, 16p + 16))
 // ---------------------------------------------------------------------------
-__device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w, int n_tiles, int warp, int lane,
-                        float c_log2, const DecodeArgs& a) {
+__device__ void build_q(uint8_t* sm, Misc& ms, const DecodeArgs& a, int b, int head_base, int heads_here,
+                        float c_log2) {
+  const int tid = threadIdx.x;
+  const int h = tid >> 2, part = tid & 3;
+  const bool live = h < heads_here;
+  const __nv_bfloat16* qrow = a.q + b * a.q_stride_b + (head_base + h) * a.q_stride_h;
+  // Two passes over this thread's 128 latent values, every load of a pass in
+  // flight at once (the rows were prefetched into L2; the second pass hits).
+  float amax = 0.f;
+  {
+    uint4 v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      v[k] = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t ws[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(ws[j] << 16)), fabsf(__uint_as_float(ws[j] & 0xFFFF0000u))));
+    }
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  // a_h = 2^(floor(log2 amax) - 7): |q / a_h| < 256 < 448 (e4m3 max)
+  int ex = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF) - 127 - 7;
+  if (amax == 0.f || ex < -126) ex = 0;
+  const float a_h = __uint_as_float(static_cast<uint32_t>(ex + 127) << 23);
+  const float inv_a = __uint_as_float(static_cast<uint32_t>(127 - ex) << 23);
+  if (part == 0) {
+    ms.ac[h] = a_h * c_log2;
+    ms.R[h] = 0.f;
+  }
+  uint8_t* qb = sm + kOffQ;
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    uint4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      v[k] = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 64 * half + 8 * k) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int k2 = 0; k2 < 8; k2 += 2) {
+    const int k = 8 * half + k2;
+    // 16 latent elements = one 16-byte core row of hi and of lo
+    uint32_t hi_w[4], lo_w[4];
+    const uint4 v0 = v[k2], v1 = v[k2 + 1];
+    const uint32_t ws[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x0 = __uint_as_float(ws[2 * j] << 16) * inv_a;
+      const float x1 = __uint_as_float(ws[2 * j] & 0xFFFF0000u) * inv_a;
+      const float x2 = __uint_as_float(ws[2 * j + 1] << 16) * inv_a;
+      const float x3 = __uint_as_float(ws[2 * j + 1] & 0xFFFF0000u) * inv_a;
+      const uint16_t h01 = cvt_f32x2_e4m3x2(x0, x1);
+      const uint16_t h23 = cvt_f32x2_e4m3x2(x2, x3);
+      const float2 g01 = e4m3x2_to_float2(h01);  // exact
+      const float2 g23 = e4m3x2_to_float2(h23);
+      const uint16_t l01 = cvt_f32x2_e4m3x2(x0 - g01.x, x1 - g01.y);
+      const uint16_t l23 = cvt_f32x2_e4m3x2(x2 - g23.x, x3 - g23.y);
+      hi_w[j] = static_cast<uint32_t>(h01) | (static_cast<uint32_t>(h23) << 16);
+      lo_w[j] = static_cast<uint32_t>(l01) | (static_cast<uint32_t>(l23) << 16);
+    }
+    const int dc = 8 * part + k / 2;  // 16-byte latent chunk of this row (0..31)
+    uint8_t* col = qb + (dc >> 3) * kVCol;
+    *reinterpret_cast<uint4*>(col + (h >> 3) * 1024 + sw128_offset(h & 7, dc & 7)) =
+        make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
+    *reinterpret_cast<uint4*>(col + (8 + (h >> 3)) * 1024 + sw128_offset(h & 7, dc & 7)) =
+        make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
+  }
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + kLatent + 16 * part + 8 * k) : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(sm + kOffQpe + (h >> 3) * kPeRow + (2 * part + k) * 128 + (h & 7) * 16) = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Softmax warps (0..7) and the per-piece epilogue
+// ---------------------------------------------------------------------------
+__device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int head_base, int heads_here,
+                        int warp, int lane, float c_log2, const DecodeArgs& a) {
   const int tid = threadIdx.x;
   const int q = warp & 3;                  // TMEM lane quadrant
   const int hf = warp >> 2;                // heads 32 hf .. 32 hf + 31
   const int st = 32 * q + lane;            // softmax token
   const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
-  const bool direct = a.num_splits == 1;
 
   float l_part[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
   int sigma_prev = 0;
-  bool aborted = false;
+  Cursor cur;
+  cursor_start(a, sc, cur);
 
-  for (int tile = 0; tile < n_tiles; ++tile) {
+  for (int tile = 0; tile < sc.count; ++tile, cursor_next(a, cur)) {
     const uint32_t par = static_cast<uint32_t>(tile & 1);
+    const bool first = cursor_first(cur);
+    if (tile > 0 && first) {
+      // a new sequence: its Q'' replaces the previous one (whose last QK is
+      // complete: its S was read), then the QK issuer may continue
+      build_q(sm, ms, a, cur.b, head_base, heads_here, c_log2);
+      fence_proxy_async_smem();
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ms.mb_qready);
+      named_bar(kBarSoftmax, kSoftmaxThreads);  // ac and R of the new sequence are visible
+    }
     // V''(j) written (for sigma of the tile), QK(j) complete
     bool ok = warp_wait(&ms.mb_vfull[tile & 1], static_cast<uint32_t>((tile >> 1) & 1), ms, a, 1, lane) &&
               warp_wait(&ms.mb_sfull, par, ms, a, 1, lane);
@@ -578,7 +887,7 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w,
       if (lane == 0) mbar_arrive(&ms.mb_sfree);
       const int sigma = ms.sig[tile & 1];
       const float sig = __uint_as_float(static_cast<uint32_t>(min(max(sigma + 127, 1), 254)) << 23);
-      const bool tvalid = st < tile_valid(w, tile);
+      const bool tvalid = st < cursor_valid(cur);
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
         const float4 ac4 = *reinterpret_cast<const float4*>(&ms.ac[32 * hf + j]);
@@ -591,21 +900,21 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w,
           t[j + u] = tvalid ? fmaf(t[j + u], acv[u] * sig, base) : -CUDART_INF_F;
         }
       }
-      // PV(j-1) must be complete before O is rescaled or P'' is overwritten
+      // PV(j-1) must be complete before O is rescaled or read, or P'' is overwritten
       if (tile > 0)
         ok = warp_wait(&ms.mb_pvdone[(tile - 1) & 1], static_cast<uint32_t>(((tile - 1) >> 1) & 1), ms, a, 2, lane);
     }
-    if (bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) {
-      aborted = true;
-      break;
-    }
-    fence_after_sync();
-    // rescale event: first tile, a score above R + 8.5, or a new sigma
+    // rescale event: a piece's first tile, a score above R + 8.5, or a new sigma.
+    // One barrier ORs "event or failure"; only when it is raised does a second
+    // one tell a failure (leave the loop) from an event.
     float tmaxv = -CUDART_INF_F;
 #pragma unroll
     for (int j = 0; j < 32; ++j) tmaxv = fmaxf(tmaxv, t[j]);
     const int sigma_cur = ms.sig[tile & 1];
-    const bool need = bar_or(kBarSoftmax, kSoftmaxThreads, tile == 0 || tmaxv > 8.5f || sigma_cur != sigma_prev);
+    const bool need =
+        bar_or(kBarSoftmax, kSoftmaxThreads, !ok || first || tmaxv > 8.5f || sigma_cur != sigma_prev);
+    if (need && bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) break;
+    fence_after_sync();
     if (need) {
       float v[32];
 #pragma unroll
@@ -614,18 +923,18 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w,
       named_bar(kBarSoftmax, kSoftmaxThreads);
       if (tid < kNH) {
         const float tm = fmaxf(fmaxf(ms.red[0][tid], ms.red[1][tid]), fmaxf(ms.red[2][tid], ms.red[3][tid]));
-        // raise R so that this tile's max maps to 2^4 (only raise; the first tile sets it)
-        const float shift = tile == 0 ? tm - 4.0f : fmaxf(tm - 4.0f, 0.0f);
+        // raise R so that this tile's max maps to 2^4 (only raise; a piece's first tile sets it)
+        const float shift = first ? tm - 4.0f : fmaxf(tm - 4.0f, 0.0f);
         const float dshift = fmaxf(shift, -1e30f);
         ms.R[tid] += dshift;
-        ms.beta[tid] = tile == 0 ? 1.0f : ex2(-dshift);
-        ms.alpha[tid] = tile == 0 ? 1.0f : ex2(-dshift + static_cast<float>(sigma_prev - sigma_cur));
+        ms.beta[tid] = first ? 1.0f : ex2(-dshift);
+        ms.alpha[tid] = first ? 1.0f : ex2(-dshift + static_cast<float>(sigma_prev - sigma_cur));
         ms.red[0][tid] = dshift;  // reused below as the per-head shift of t
       }
       named_bar(kBarSoftmax, kSoftmaxThreads);
 #pragma unroll
       for (int j = 0; j < 32; ++j) t[j] -= ms.red[0][32 * hf + j];
-      if (tile > 0) {
+      if (!first) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) l_part[j] *= ms.beta[32 * hf + j];
 #pragma unroll 1
@@ -678,56 +987,64 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const WorkItem& w,
     fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(&ms.mb_pfull);
-  }
 
-  // ---------------- epilogue ----------------
-  if (!aborted) {
-    const bool ok = warp_wait(&ms.mb_pvdone[(n_tiles - 1) & 1], static_cast<uint32_t>(((n_tiles - 1) >> 1) & 1),
-                              ms, a, 4, lane);
-    aborted = bar_or(kBarSoftmax, kSoftmaxThreads, !ok);
-  }
-  if (aborted) return;
-  fence_after_sync();
-  {
-    const float s = warp_transpose_reduce<false>(l_part, lane);
-    ms.red[q][32 * hf + lane] = s;
-  }
-  named_bar(kBarSoftmax, kSoftmaxThreads);
-  if (tid < kNH) {
-    const float l = ms.red[0][tid] + ms.red[1][tid] + ms.red[2][tid] + ms.red[3][tid];
-    // output factor 2^sigma / l per head (alpha is free again)
-    ms.alpha[tid] = l > 0.f ? exp2f(static_cast<float>(sigma_prev)) / l : 0.f;
-    if (!direct && tid < w.heads_here) {
-      const int64_t row = (static_cast<int64_t>(w.b) * a.num_splits + w.split) * a.num_heads + w.head_base + tid;
-      a.partial_lse[row] = (ms.R[tid] + __log2f(l)) * kLn2;
+    if (!cursor_last(cur)) continue;
+    // ---------------- epilogue of the piece ----------------
+    const bool done = warp_wait(&ms.mb_pvdone[tile & 1], static_cast<uint32_t>((tile >> 1) & 1), ms, a, 4, lane);
+    if (bar_or(kBarSoftmax, kSoftmaxThreads, !done)) break;
+    fence_after_sync();
+    {
+      const float s = warp_transpose_reduce<false>(l_part, lane);
+      ms.red[q][32 * hf + lane] = s;
     }
-  }
-  named_bar(kBarSoftmax, kSoftmaxThreads);
-  // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane
-#pragma unroll 1
-  for (int cc = 0; cc < 2; ++cc) {
-    const int c = 2 * hf + cc;
-    const int d = 128 * c + 32 * q + lane;
-#pragma unroll 1
-    for (int hh = 0; hh < 2; ++hh) {
-      uint32_t vv[32];
-      tmem_ld32(tmem + lane_base + kColO + 64 * c + 32 * hh, vv);
-      tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int h = 32 * hh + j;
-        if (h < w.heads_here) {
-          const float val = __uint_as_float(vv[j]) * ms.alpha[h];
-          const int hq = w.head_base + h;
-          if (direct) {
-            a.o[w.b * a.o_stride_b + hq * a.o_stride_h + d] = __float2bfloat16_rn(val);
-          } else {
-            const int64_t row = (static_cast<int64_t>(w.b) * a.num_splits + w.split) * a.num_heads + hq;
-            a.partial_o[row * kLatent + d] = val;
+    for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
+    // the piece covers its whole sequence -> final output; otherwise a partial in its slot
+    const bool direct = a.balanced ? (cur.piece_begin == 0 && cur.piece_end == cursor_tiles(cur))
+                                   : a.num_splits == 1;
+    const int64_t slot = a.balanced ? static_cast<int64_t>(cur.b) + blockIdx.x
+                                    : static_cast<int64_t>(cur.b) * a.num_splits + blockIdx.x;
+    named_bar(kBarSoftmax, kSoftmaxThreads);
+    if (tid < kNH) {
+      const float l = ms.red[0][tid] + ms.red[1][tid] + ms.red[2][tid] + ms.red[3][tid];
+      // output factor 2^sigma / l per head (alpha is free again)
+      ms.alpha[tid] = l > 0.f ? exp2f(static_cast<float>(sigma_prev)) / l : 0.f;
+      if (!direct && tid < heads_here)
+        a.partial_lse[slot * a.num_heads + head_base + tid] = (ms.R[tid] + __log2f(l)) * kLn2;
+    }
+    if (a.balanced && tid == 0 && cur.piece_begin == 0) {
+      // this CTA holds the sequence's first tile: record its CTA span for the merge
+      const int last_cta = cta_of_tile(cur.seq_pos + cursor_tiles(cur) - 1, sc, gridDim.x);
+      a.seq_meta[cur.b] = make_int2(blockIdx.x, last_cta);
+    }
+    named_bar(kBarSoftmax, kSoftmaxThreads);
+    // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane
+#pragma unroll 1
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 2 * hf + cc;
+      const int d = 128 * c + 32 * q + lane;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t vv[32];
+        tmem_ld32(tmem + lane_base + kColO + 64 * c + 32 * hh, vv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int h = 32 * hh + j;
+          if (h < heads_here) {
+            const float val = __uint_as_float(vv[j]) * ms.alpha[h];
+            const int hq = head_base + h;
+            if (direct)
+              a.o[cur.b * a.o_stride_b + hq * a.o_stride_h + d] = __float2bfloat16_rn(val);
+            else
+              a.partial_o[(slot * a.num_heads + hq) * kLatent + d] = __float2bfloat16_rn(val);
           }
         }
       }
     }
+    // O and alpha are read before the next piece's PV / rescale touch them
+    fence_before_sync();
+    named_bar(kBarSoftmax, kSoftmaxThreads);
   }
 }
 
@@ -737,137 +1054,86 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __gr
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  const int head_base = blockIdx.z * kNH;
+  const int heads_here = min(kNH, a.num_heads - head_base);
 
-  WorkItem w;
-  w.split = blockIdx.x;
-  w.b = blockIdx.y;
-  w.head_base = blockIdx.z * kNH;
-  w.heads_here = min(kNH, a.num_heads - w.head_base);
-  w.page_lo = a.kv_indptr[w.b];
-  w.n_pages = max(a.kv_indptr[w.b + 1] - w.page_lo, 0);
-  const int last_len =
-      w.n_pages == 0 ? 0 : min(max(a.kv_last_page_len ? a.kv_last_page_len[w.b] : kPageSize, 1), kPageSize);
-  w.n_tok = w.n_pages == 0 ? 0 : (w.n_pages - 1) * kPageSize + last_len;
-  const int pps = 2 * ((w.n_pages + 2 * a.num_splits - 1) / (2 * a.num_splits));
-  w.p_begin = w.split * pps;
-  w.p_end = min(w.p_begin + pps, w.n_pages);
-  const bool direct = a.num_splits == 1;
-
-  if (w.p_begin >= w.p_end) {
-    if (direct) {
-      for (int i = tid; i < w.heads_here * (kLatent / 2); i += kThreadsTC) {
-        const int h = i / (kLatent / 2), d = (i % (kLatent / 2)) * 2;
-        *reinterpret_cast<uint32_t*>(a.o + w.b * a.o_stride_b + (w.head_base + h) * a.o_stride_h + d) = 0u;
-      }
-    } else if (tid < w.heads_here) {
-      a.partial_lse[(static_cast<int64_t>(w.b) * a.num_splits + w.split) * a.num_heads + w.head_base + tid] =
-          -CUDART_INF_F;
+  Sched sc;
+  if (a.balanced) {
+    balanced_schedule(a, ms, sc);
+    if (sc.count == 0) {
+      // An empty run (fewer tiles than CTAs) can sit inside the CTA span of
+      // the sequence at its position; its slot of that sequence carries no weight.
+      if (sc.pos0 < sc.total && tid < heads_here)
+        a.partial_lse[(static_cast<int64_t>(sc.b0) + blockIdx.x) * a.num_heads + head_base + tid] = -CUDART_INF_F;
+      return;  // (uniform: every thread read the same count)
     }
-    return;
+  } else {
+    const int b = blockIdx.y, tiles = seq_tiles_of(a, b);
+    const int per_split = (tiles + a.num_splits - 1) / a.num_splits;
+    sc.b0 = b;
+    sc.off0 = blockIdx.x * per_split;
+    sc.count = max(0, min(per_split, tiles - sc.off0));
+    sc.pos0 = 0;
+    sc.total = 0;
+    sc.per_seq = sc.split_tiles = sc.seq_tiles = 0;
+    if (sc.count == 0) {
+      // nothing to attend to: zeros (one split) or a split that carries no weight
+      if (a.num_splits == 1) {
+        for (int i = tid; i < heads_here * (kLatent / 2); i += kThreadsTC) {
+          const int h = i / (kLatent / 2), d = (i % (kLatent / 2)) * 2;
+          *reinterpret_cast<uint32_t*>(a.o + b * a.o_stride_b + (head_base + h) * a.o_stride_h + d) = 0u;
+        }
+      } else if (tid < heads_here) {
+        a.partial_lse[(static_cast<int64_t>(b) * a.num_splits + blockIdx.x) * a.num_heads + head_base + tid] =
+            -CUDART_INF_F;
+      }
+      return;
+    }
   }
-  const int n_tiles = (w.p_end - w.p_begin + 1) / 2;
   const float c_log2 = a.sm_scale * kLog2e;
 
-  // ---------------- setup: TMEM, barriers, Q operands ----------------
-  if (warp == kWarpQK) {
-    tmem_alloc(&ms.tmem_base, kTmemCols);
-    if (lane == 0) {
-      mbar_init(&ms.mb_vfull[0], 4);
-      mbar_init(&ms.mb_vfull[1], 4);
-      mbar_init(&ms.mb_pvdone[0], kPvIssuers);
-      mbar_init(&ms.mb_pvdone[1], kPvIssuers);
-      mbar_init(&ms.mb_sfull, 1);
-      mbar_init(&ms.mb_sfree, kSoftmaxWarps);
-      mbar_init(&ms.mb_pfull, kSoftmaxWarps);
-      mbar_init(&ms.mb_drain, 1 + kPvIssuers);
-      fence_mbar_init();
-      ms.abort_flag = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ms.tile_smax[i] = 0;
-    }
-  } else if (warp < kSoftmaxWarps) {
-    // 4 threads per head: part p handles latent [128p, 128p + 128) and RoPE [16p, 16p + 16).
-    const int h = tid >> 2, part = tid & 3;
-    const bool live = h < w.heads_here;
-    const __nv_bfloat16* qrow = a.q + w.b * a.q_stride_b + (w.head_base + h) * a.q_stride_h;
-    // two passes over this thread's 128 latent values (the second hits in cache)
-    float amax = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < 16; ++k) {
-      const uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k) : make_uint4(0, 0, 0, 0);
-      const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(ws[j] << 16)), fabsf(__uint_as_float(ws[j] & 0xFFFF0000u))));
-    }
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    // a_h = 2^(floor(log2 amax) - 7): |q / a_h| < 256 < 448 (e4m3 max)
-    int ex = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF) - 127 - 7;
-    if (amax == 0.f || ex < -126) ex = 0;
-    const float a_h = __uint_as_float(static_cast<uint32_t>(ex + 127) << 23);
-    const float inv_a = __uint_as_float(static_cast<uint32_t>(127 - ex) << 23);
-    if (part == 0) {
-      ms.ac[h] = a_h * c_log2;
-      ms.R[h] = 0.f;
-    }
-    uint8_t* qb = sm + kOffQ;
-#pragma unroll 1
-    for (int k = 0; k < 16; k += 2) {
-      // 16 latent elements = one 16-byte core row of hi and of lo
-      uint32_t hi_w[4], lo_w[4];
-      const uint4 v0 = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k) : make_uint4(0, 0, 0, 0);
-      const uint4 v1 = live ? *reinterpret_cast<const uint4*>(qrow + 128 * part + 8 * k + 8) : make_uint4(0, 0, 0, 0);
-      const uint32_t ws[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float x0 = __uint_as_float(ws[2 * j] << 16) * inv_a;
-        const float x1 = __uint_as_float(ws[2 * j] & 0xFFFF0000u) * inv_a;
-        const float x2 = __uint_as_float(ws[2 * j + 1] << 16) * inv_a;
-        const float x3 = __uint_as_float(ws[2 * j + 1] & 0xFFFF0000u) * inv_a;
-        const uint16_t h01 = cvt_f32x2_e4m3x2(x0, x1);
-        const uint16_t h23 = cvt_f32x2_e4m3x2(x2, x3);
-        const float2 g01 = e4m3x2_to_float2(h01);  // exact
-        const float2 g23 = e4m3x2_to_float2(h23);
-        const uint16_t l01 = cvt_f32x2_e4m3x2(x0 - g01.x, x1 - g01.y);
-        const uint16_t l23 = cvt_f32x2_e4m3x2(x2 - g23.x, x3 - g23.y);
-        hi_w[j] = static_cast<uint32_t>(h01) | (static_cast<uint32_t>(h23) << 16);
-        lo_w[j] = static_cast<uint32_t>(l01) | (static_cast<uint32_t>(l23) << 16);
-      }
-      const int dc = 8 * part + k / 2;  // 16-byte latent chunk of this row (0..31)
-      uint8_t* col = qb + (dc >> 3) * kVCol;
-      *reinterpret_cast<uint4*>(col + (h >> 3) * 1024 + sw128_offset(h & 7, dc & 7)) =
-          make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
-      *reinterpret_cast<uint4*>(col + (8 + (h >> 3)) * 1024 + sw128_offset(h & 7, dc & 7)) =
-          make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
-    }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + kLatent + 16 * part + 8 * k) : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(sm + kOffQpe + (h >> 3) * kPeRow + (2 * part + k) * 128 + (h & 7) * 16) = v;
-    }
-  }
-  fence_proxy_async_smem();
-  fence_before_sync();
-  __syncthreads();
-  fence_after_sync();
-  const uint32_t tmem = ms.tmem_base;
-
+  // ---------------- setup: TMEM, barriers, Q'' of the first sequence ----------------
+  // Register budgets first (the loaders' increase waits for the issuers' decrease),
+  // then each role sets up its part and meets the others at the setup barrier.
   if (warp >= kWarpQK) {
     setmaxnreg_dec<kIssuerRegs>();
+    if (warp == kWarpQK) {
+      tmem_alloc(&ms.tmem_base, kTmemCols);
+      if (lane == 0) {
+        mbar_init(&ms.mb_vfull[0], 4);
+        mbar_init(&ms.mb_vfull[1], 4);
+        mbar_init(&ms.mb_pvdone[0], kPvIssuers);
+        mbar_init(&ms.mb_pvdone[1], kPvIssuers);
+        mbar_init(&ms.mb_sfull, 1);
+        mbar_init(&ms.mb_sfree, kSoftmaxWarps);
+        mbar_init(&ms.mb_pfull, kSoftmaxWarps);
+        mbar_init(&ms.mb_drain, 1 + kPvIssuers);
+        mbar_init(&ms.mb_qready, kSoftmaxWarps);
+        fence_mbar_init();
+        ms.abort_flag = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ms.tile_smax[i] = 0;
+      }
+    }
+    setup_barrier();
+    const uint32_t tmem = ms.tmem_base;
     const bool issuer = warp < kWarpPV0 + kPvIssuers;
     if (warp == kWarpQK)
-      qk_issuer(sm, ms, tmem, n_tiles, lane, a);
+      qk_issuer(sm, ms, tmem, sc, lane, a);
     else if (issuer)
-      pv_issuer(sm, ms, tmem, n_tiles, lane, warp - kWarpPV0, a);
+      pv_issuer(sm, ms, tmem, sc, lane, warp - kWarpPV0, a);
     // drain: arrives once every MMA this thread issued has completed
     if (issuer && lane == 0) mma_commit(&ms.mb_drain);
     __syncwarp();
   } else if (warp >= kLoaderWarp0) {
     setmaxnreg_inc<kLoaderRegs>();
-    loader(sm, ms, tmem, w, n_tiles, warp - kLoaderWarp0, lane, a);
+    loader(sm, ms, sc, head_base, heads_here, warp - kLoaderWarp0, lane, a);
   } else {
-    softmax(sm, ms, tmem, w, n_tiles, warp, lane, c_log2, a);
+    prefetch_q(a, sc.b0, head_base, heads_here, tid, kSoftmaxThreads);
+    build_q(sm, ms, a, sc.b0, head_base, heads_here, c_log2);
+    fence_proxy_async_smem();
+    setup_barrier();
+    softmax(sm, ms, ms.tmem_base, sc, head_base, heads_here, warp, lane, c_log2, a);
   }
 
   fence_before_sync();
@@ -876,7 +1142,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __gr
     if (lane == 0 && !mbar_wait_bounded(&ms.mb_drain, 0, kPollLimit)) record_status(a, 128);
     __syncwarp();
     fence_after_sync();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(ms.tmem_base, kTmemCols);
   }
 }
 
@@ -885,7 +1151,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1) mla_decode_tc_kernel(const __gr
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(mla_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTC);
   if (e != cudaSuccess) return e;
-  const dim3 grid(a.num_splits, a.batch, (a.num_heads + kNH - 1) / kNH);
+  const int head_blocks = (a.num_heads + kNH - 1) / kNH;
+  const dim3 grid = a.balanced ? dim3(a.num_splits, 1, head_blocks) : dim3(a.num_splits, a.batch, head_blocks);
   mla_decode_tc_kernel<<<grid, kThreadsTC, kSmemTC, stream>>>(a);
   return cudaGetLastError();
 }

@@ -8,8 +8,14 @@
 // rows are never read.
 //
 // One 128-thread CTA per (sequence, head): each thread owns 4 consecutive
-// latent columns (one float4 per split), so every partial row is read once,
+// latent columns (four values per split: bf16 partials from this library's
+// decode, fp32 ones through kimi_mla_reduce), so every partial row is read once,
 // fully coalesced; the kernel is bound by HBM reads of the partials.
+//
+// Split mode: the partials of sequence b are slots b * num_splits + s.
+// Balanced mode (seq_meta set): they are slots b + c for the CTAs c in
+// [meta.x, meta.y] that held b's tiles; a sequence held by one CTA was written
+// by the decode kernel itself and is skipped, one without pages gets zeros.
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
@@ -22,18 +28,37 @@ __global__ void __launch_bounds__(128) mla_reduce_kernel(ReduceArgs a) {
   const int b = blockIdx.y;
   const int h = blockIdx.x;
   const int d = threadIdx.x * 4;
-  const int64_t lse_base = static_cast<int64_t>(b) * a.num_splits * a.num_heads + h;
+  int64_t first_slot = static_cast<int64_t>(b) * a.num_splits;
+  int n_slots = a.num_splits;
+  if (a.seq_meta) {
+    if (a.kv_indptr[b + 1] <= a.kv_indptr[b]) {
+      *reinterpret_cast<uint2*>(a.o + b * a.o_stride_b + h * a.o_stride_h + d) = make_uint2(0u, 0u);
+      return;
+    }
+    const int2 span = a.seq_meta[b];
+    if (span.x == span.y) return;
+    first_slot = static_cast<int64_t>(b) + span.x;
+    n_slots = span.y - span.x + 1;
+  }
+  const int64_t lse_base = first_slot * a.num_heads + h;
   float m = -CUDART_INF_F;
-  for (int s = 0; s < a.num_splits; ++s) m = fmaxf(m, a.partial_lse[lse_base + s * a.num_heads]);
+  for (int s = 0; s < n_slots; ++s) m = fmaxf(m, a.partial_lse[lse_base + s * a.num_heads]);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float wsum = 0.f;
   if (m != -CUDART_INF_F) {
-    for (int s = 0; s < a.num_splits; ++s) {
+    for (int s = 0; s < n_slots; ++s) {
       const float l = a.partial_lse[lse_base + s * a.num_heads];
       if (l == -CUDART_INF_F) continue;
       const float w = __expf(l - m);
-      const float4 v = *reinterpret_cast<const float4*>(
-          a.partial_o + (lse_base + static_cast<int64_t>(s) * a.num_heads) * kLatent + d);
+      const int64_t off = (lse_base + static_cast<int64_t>(s) * a.num_heads) * kLatent + d;
+      float4 v;
+      if (a.partial_bf16) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.partial_o) + off);
+        v = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u),
+                        __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xFFFF0000u));
+      } else {
+        v = *reinterpret_cast<const float4*>(static_cast<const float*>(a.partial_o) + off);
+      }
       acc.x += w * v.x;
       acc.y += w * v.y;
       acc.z += w * v.z;

@@ -200,12 +200,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (issuing nothing) until the phase completes or about `ns`
+// nanoseconds pass, instead of spinning through quick polls.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* mbar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(mbar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Each unsuccessful poll of the bounded waits below sleeps up to this long.
+constexpr uint32_t kWaitSleepNs = 20000;
+
 // Wait for the phase with the given parity to complete, giving up after
-// `max_polls` unsuccessful polls (each try_wait itself blocks for a
-// hardware-defined interval).  Returns false on give-up.
+// `max_polls` unsuccessful polls (each sleeping up to kWaitSleepNs).  Returns
+// false on give-up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* mbar, uint32_t parity, uint32_t max_polls) {
   for (uint32_t i = 0; i < max_polls; ++i)
-    if (mbar_try_wait(mbar, parity)) return true;
+    if (mbar_try_wait_sleep(mbar, parity, kWaitSleepNs)) return true;
   return false;
 }
 
@@ -214,8 +232,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* mbar, uint32_t parit
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* mbar, uint32_t parity, uint32_t max_polls,
                                                    const volatile int* abort) {
   for (uint32_t i = 0; i < max_polls; ++i) {
-    if (mbar_try_wait(mbar, parity)) return true;
-    if ((i & 63u) == 63u && *abort) return false;
+    if (mbar_try_wait_sleep(mbar, parity, kWaitSleepNs)) return true;
+    if (*abort) return false;
   }
   return false;
 }

@@ -105,23 +105,9 @@ def _default_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return buf
 
 
-def mla_decode_fwd(q: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Tensor, o: torch.Tensor,
-                   qo_indptr: torch.Tensor | None, kv_indptr: torch.Tensor, kv_indices: torch.Tensor,
-                   kv_last_page_len: torch.Tensor | None, max_seqlen_q: int = 1, page_size: int = PAGE_SIZE,
-                   nhead_kv: int = 1, sm_scale: float | None = None, logit_cap: float = 0.0,
-                   num_kv_splits: int | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Absorbed-MLA decode over the paged MXFP4 latent cache; writes ``o``.
-
-    q            bf16 [batch, num_heads, 576] (rows may be strided; last dim contiguous)
-    kv_buffer    uint8 [num_pages, 64, 384] (nibbles of the 512-dim latent, then bf16 RoPE)
-    kv_scales    uint8 [num_pages, 64, 16]  (e8m0, one per 32 latent elements)
-    o            bf16 [batch, num_heads, 512], any (batch, head) strides
-    kv_indptr    int32 [batch + 1] page offsets; kv_indices int32 page ids;
-    kv_last_page_len int32 [batch] tokens in each last page (None = full pages)
-    sm_scale     softmax scale (default 1/sqrt(576))
-    num_kv_splits split-K count (None = automatic); workspace optional uint8
-                 buffer of at least :func:`workspace_bytes`
-    """
+def _run_decode(entry: str, q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
+                max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits, workspace):
+    """Checks the arguments, fills the C-ABI params and calls ``entry``."""
     dev = _require_cuda(q, kv_buffer, kv_scales, o, kv_indptr, kv_indices)
     if max_seqlen_q != 1:
         raise ValueError("mla_decode_fwd supports one query token per sequence (max_seqlen_q == 1)")
@@ -169,9 +155,55 @@ def mla_decode_fwd(q: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Te
     ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
     ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
     with torch.cuda.device(dev):
-        status = lib.kimi_mla_decode(ctypes.byref(p), ws_ptr, ws_bytes, _stream_handle(dev))
-    _lib.check(status, "kimi_mla_decode")
+        status = getattr(lib, entry)(ctypes.byref(p), ws_ptr, ws_bytes, _stream_handle(dev))
+    _lib.check(status, entry)
     return o
+
+
+def mla_decode_fwd(q: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Tensor, o: torch.Tensor,
+                   qo_indptr: torch.Tensor | None, kv_indptr: torch.Tensor, kv_indices: torch.Tensor,
+                   kv_last_page_len: torch.Tensor | None, max_seqlen_q: int = 1, page_size: int = PAGE_SIZE,
+                   nhead_kv: int = 1, sm_scale: float | None = None, logit_cap: float = 0.0,
+                   num_kv_splits: int | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Absorbed-MLA decode over the paged MXFP4 latent cache; writes ``o``.
+
+    q            bf16 [batch, num_heads, 576] (rows may be strided; last dim contiguous)
+    kv_buffer    uint8 [num_pages, 64, 384] (nibbles of the 512-dim latent, then bf16 RoPE)
+    kv_scales    uint8 [num_pages, 64, 16]  (e8m0, one per 32 latent elements)
+    o            bf16 [batch, num_heads, 512], any (batch, head) strides
+    kv_indptr    int32 [batch + 1] page offsets; kv_indices int32 page ids;
+    kv_last_page_len int32 [batch] tokens in each last page (None = full pages)
+    sm_scale     softmax scale (default 1/sqrt(576))
+    num_kv_splits equal split-K ranges per sequence (the reference's meaning),
+                 or None / 0 for the balanced schedule over all SMs;
+                 workspace optional uint8 buffer of at least :func:`workspace_bytes`
+    """
+    return _run_decode("kimi_mla_decode", q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices,
+                       kv_last_page_len, max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits,
+                       workspace)
+
+
+def mla_decode_partial(q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
+                       max_seqlen_q: int = 1, page_size: int = PAGE_SIZE, nhead_kv: int = 1,
+                       sm_scale: float | None = None, logit_cap: float = 0.0, num_kv_splits: int | None = None,
+                       workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The split-K attention launch of :func:`mla_decode_fwd` alone (the
+    archive's ``_mla_decode_split_kv``); pair it with :func:`mla_decode_merge`
+    on the same arguments and workspace."""
+    return _run_decode("kimi_mla_decode_partial", q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices,
+                       kv_last_page_len, max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits,
+                       workspace)
+
+
+def mla_decode_merge(q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
+                     max_seqlen_q: int = 1, page_size: int = PAGE_SIZE, nhead_kv: int = 1,
+                     sm_scale: float | None = None, logit_cap: float = 0.0, num_kv_splits: int | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The log-sum-exp merge launch of :func:`mla_decode_fwd` alone (the
+    archive's ``_mla_reduce``), after :func:`mla_decode_partial`."""
+    return _run_decode("kimi_mla_decode_merge", q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices,
+                       kv_last_page_len, max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits,
+                       workspace)
 
 
 def mla_reduce(partial_o: torch.Tensor, partial_lse: torch.Tensor, o: torch.Tensor) -> torch.Tensor:

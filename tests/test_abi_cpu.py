@@ -37,16 +37,29 @@ def test_status_strings_and_version():
 
 def test_workspace_size_arithmetic():
     lib = _lib.load()
-    # explicit splits: partial O (B*S*H*512 f32) + LSE (B*S*H f32), each rounded to 256 B
+    # explicit splits: partial O (B*S*H*512 bf16) + LSE (B*S*H f32), each rounded to 256 B
     b, h, s = 64, 64, 4
     rows = b * s * h
-    expect = ((rows * 512 * 4 + 255) // 256) * 256 + ((rows * 4 + 255) // 256) * 256
+    expect = ((rows * 512 * 2 + 255) // 256) * 256 + ((rows * 4 + 255) // 256) * 256
     assert lib.kimi_mla_decode_workspace_size(b, h, s) == expect
     assert lib.kimi_mla_decode_workspace_size(b, h, 1) == 0  # single split writes o directly
     assert lib.kimi_mla_decode_workspace_size(b, 0, 4) == 0  # invalid
     assert lib.kimi_mla_decode_num_splits(b, h, 7) == 7
     assert lib.kimi_mla_decode_num_splits(b, h, 999) == 64
-    assert 1 <= lib.kimi_mla_decode_num_splits(2, 16, 0) <= 32
+
+
+def test_balanced_workspace_size_arithmetic():
+    # num_kv_splits = 0: balanced schedule over G CTAs per 64-head block; the
+    # workspace holds B + G partial slots plus one int2 CTA span per sequence
+    lib = _lib.load()
+    for b, h in ((64, 64), (2, 16), (8, 128)):
+        g = lib.kimi_mla_decode_num_splits(b, h, 0)
+        assert g >= 1
+        slots = b + g
+        r256 = lambda n: ((n + 255) // 256) * 256
+        expect = r256(slots * h * 512 * 2) + r256(slots * h * 4) + r256(b * 8)
+        assert lib.kimi_mla_decode_workspace_size(b, h, 0) == expect
+    assert lib.kimi_mla_decode_num_splits(8, 128, 0) * 2 <= lib.kimi_mla_decode_num_splits(8, 64, 0) + 1
 
 
 def test_decode_rejects_bad_arguments_on_host():

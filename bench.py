@@ -9,6 +9,13 @@ library's KV-append quantiser).  A step is one decode call over the whole
 batch (one layer).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload kimi_k2|ragged]
+
+``--workload ragged`` runs the batch-sharded sweep instead: one batch of 256
+sequences with lengths drawn uniformly from 1K-32K tokens (seeded), spread
+over the N ranks by longest-first bin packing (kimi_b200.dp), each rank
+holding only its sequences' pages; the whole batch is fixed as N grows
+(strong scaling) and the gather of the outputs to rank 0 is timed separately.
 
 Prints one JSON line on rank 0.  ``value`` is the aggregate achieved HBM
 bandwidth over all ranks computed from the algorithmic bytes (latent nibbles
@@ -122,6 +129,52 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+RAGGED_BATCH, RAGGED_MIN, RAGGED_MAX, RAGGED_SEED = 256, 1024, 32768, 3
+RAGGED_WORKLOAD = (f"batch-sharded MXFP4 MLA decode: {HEADS} heads, one batch of {RAGGED_BATCH} sequences, ctx "
+                   f"uniform {RAGGED_MIN}-{RAGGED_MAX} (seed {RAGGED_SEED}), page {PAGE}, shuffled pages, "
+                   f"longest-first bin packing over the ranks, num_kv_splits auto")
+
+
+def ragged_lengths():
+    import numpy as np
+    rng = np.random.default_rng(RAGGED_SEED)
+    return [int(x) for x in rng.integers(RAGGED_MIN, RAGGED_MAX + 1, RAGGED_BATCH)]
+
+
+def build_ragged_workload(torch, kimi, dev, rank: int, world: int):
+    """This rank's share of the ragged batch: its sequences' pages only."""
+    from kimi_b200 import dp
+    lens = ragged_lengths()
+    shards = dp.shard_sequences(lens, world)
+    mine = shards[rank]
+    gen = torch.Generator(device=dev).manual_seed(RAGGED_SEED * 1000 + rank)
+    local_lens = [lens[i] for i in mine]
+    pages_per = [(n + PAGE - 1) // PAGE for n in local_lens]
+    pages = max(sum(pages_per), 1)
+    kvb, kvs = kimi.alloc_mxfp4_cache(pages, dev, zero=False)
+    chunk = 1 << 16
+    for start in range(0, pages * PAGE, chunk):
+        n = min(chunk, pages * PAGE - start)
+        kv_c = torch.randn(n, 512, generator=gen, device=dev).to(torch.bfloat16)
+        k_pe = torch.randn(n, 64, generator=gen, device=dev).to(torch.bfloat16)
+        kimi.mxfp4_kv_append(kv_c, k_pe, kvb, kvs, torch.arange(start, start + n, device=dev))
+    perm = torch.randperm(pages, generator=gen, device=dev).to(torch.int32)
+    indptr = torch.zeros(len(mine) + 1, dtype=torch.int32)
+    indptr[1:] = torch.cumsum(torch.tensor(pages_per, dtype=torch.int32), 0) if mine else indptr[1:]
+    last = torch.tensor([n - (p - 1) * PAGE for n, p in zip(local_lens, pages_per)], dtype=torch.int32)
+    qgen = torch.Generator(device=dev).manual_seed(RAGGED_SEED)
+    q_all = torch.randn(RAGGED_BATCH, HEADS, 576, generator=qgen, device=dev).to(torch.bfloat16)
+    idx = torch.tensor(mine, dtype=torch.long, device=dev)
+    q = q_all[idx].contiguous()
+    o = torch.empty(len(mine), HEADS, 512, dtype=torch.bfloat16, device=dev)
+    ws = kimi.alloc_workspace(max(len(mine), 1), HEADS, None, dev)
+    tokens_local = sum(local_lens)
+    return dict(kvb=kvb, kvs=kvs, perm=perm, indptr=indptr.to(dev), last=last.to(dev), q=q, o=o, ws=ws,
+                shards=shards, lens=lens, batch=len(mine),
+                bytes_local=tokens_local * TOKEN_BYTES_ALGO + len(mine) * HEADS * 576 * 2,
+                bytes_total=sum(lens) * TOKEN_BYTES_ALGO + RAGGED_BATCH * HEADS * 576 * 2)
+
+
 def build_workload(torch, kimi, dev, seed: int):
     gen = torch.Generator(device=dev).manual_seed(seed)
     pages = BATCH * CTX // PAGE
@@ -139,7 +192,7 @@ def build_workload(torch, kimi, dev, seed: int):
     o_hf = torch.empty(HEADS, BATCH, 512, dtype=torch.bfloat16, device=dev)
     ws = kimi.alloc_workspace(BATCH, HEADS, None, dev)
     return dict(kvb=kvb, kvs=kvs, perm=perm, indptr=indptr, last=last, q=q, o_hf=o_hf, o=o_hf.permute(1, 0, 2),
-                ws=ws)
+                ws=ws, batch=BATCH)
 
 
 def run_ours(args, rank, world, local_rank):
@@ -150,13 +203,18 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    # Two independent caches (2 x 210 MB > 126 MB L2), alternated step by step.
-    wl = [build_workload(torch, kimi, dev, seed=1000 * rank + s) for s in (1, 2)]
-    splits = kimi.num_kv_splits_for(BATCH, HEADS, None)
+    ragged = args.workload == "ragged"
+    if ragged:
+        # one cache of ~1.7 GB / N per rank (far larger than the 126 MB L2)
+        wl = [build_ragged_workload(torch, kimi, dev, rank, world)]
+    else:
+        # Two independent caches (2 x 210 MB > 126 MB L2), alternated step by step.
+        wl = [build_workload(torch, kimi, dev, seed=1000 * rank + s) for s in (1, 2)]
+    splits = kimi.num_kv_splits_for(wl[0]["batch"], HEADS, None)
     stream = torch.cuda.current_stream(dev)
 
     def step(i):
-        w = wl[i & 1]
+        w = wl[i % len(wl)]
         kimi.mla_decode_fwd(w["q"], w["kvb"], w["kvs"], w["o"], None, w["indptr"], w["perm"], w["last"],
                             sm_scale=SM_SCALE, workspace=w["ws"])
 
@@ -191,7 +249,7 @@ def run_ours(args, rank, world, local_rank):
         # ---- per-launch durations: events around each stage-1 launch and each merge ----
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * args.steps)]
         for i in range(args.steps):
-            w = wl[i & 1]
+            w = wl[i % len(wl)]
             call = (w["q"], w["kvb"], w["kvs"], w["o"], None, w["indptr"], w["perm"], w["last"])
             ev[3 * i].record(stream)
             kimi.mla_decode_partial(*call, sm_scale=SM_SCALE, workspace=w["ws"])
@@ -208,7 +266,7 @@ def run_ours(args, rank, world, local_rank):
             qh.copy_(w["q"].cpu())
         meta_host = [(w["indptr"].cpu().pin_memory(), w["perm"].cpu().pin_memory(), w["last"].cpu().pin_memory())
                      for w in wl]
-        o_host = torch.empty(BATCH, HEADS, 512, dtype=torch.bfloat16).pin_memory()
+        o_host = torch.empty(wl[0]["batch"], HEADS, 512, dtype=torch.bfloat16).pin_memory()
         dev_meta = [(torch.empty_like(w["indptr"]), torch.empty_like(w["perm"]), torch.empty_like(w["last"]))
                     for w in wl]
         h2d = q_host[0].numel() * 2 + sum(t.numel() * 4 for t in meta_host[0])
@@ -218,8 +276,9 @@ def run_ours(args, rank, world, local_rank):
         e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e2.record(stream)
         for i in range(args.steps):
-            w, (ip_h, px_h, la_h), (ip_d, px_d, la_d) = wl[i & 1], meta_host[i & 1], dev_meta[i & 1]
-            w["q"].copy_(q_host[i & 1], non_blocking=True)
+            k = i % len(wl)
+            w, (ip_h, px_h, la_h), (ip_d, px_d, la_d) = wl[k], meta_host[k], dev_meta[k]
+            w["q"].copy_(q_host[k], non_blocking=True)
             ip_d.copy_(ip_h, non_blocking=True)
             px_d.copy_(px_h, non_blocking=True)
             la_d.copy_(la_h, non_blocking=True)
@@ -231,29 +290,57 @@ def run_ours(args, rank, world, local_rank):
         barrier()
         e2e_ms = max_over_ranks(e2.elapsed_time(e3))
 
-    nbytes = algorithmic_bytes()
+    # the gather of the outputs to rank 0 (ragged workload), timed on its own
+    gather_ms = None
+    if ragged:
+        from kimi_b200 import dp
+        w = wl[0]
+        for _ in range(3):
+            dp.gather_outputs(w["o"], w["shards"], rank, world, batch=RAGGED_BATCH)
+        torch.cuda.synchronize()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        g0.record(stream)
+        for _ in range(reps):
+            dp.gather_outputs(w["o"], w["shards"], rank, world, batch=RAGGED_BATCH)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gather_ms = max_over_ranks(g0.elapsed_time(g1) / reps)
+    nbytes = wl[0]["bytes_local"] if ragged else algorithmic_bytes()
+    nbytes_job = wl[0]["bytes_total"] if ragged else world * nbytes
     ms_step = ms_total / args.steps
     stage1_avg = sum(stage1_ms) / len(stage1_ms)
     red_ms = sum(merge_ms) / len(merge_ms)
-    value_tbs = world * nbytes / (ms_step * 1e-3) / 1e12
-    e2e_tbs = world * nbytes / (e2e_ms / args.steps * 1e-3) / 1e12
+    value_tbs = nbytes_job / (ms_step * 1e-3) / 1e12
+    e2e_tbs = nbytes_job / (e2e_ms / args.steps * 1e-3) / 1e12
     peak, peak_kind = _peak_hbm()
     achieved_gbs = nbytes / (stage1_avg * 1e-3) / 1e9
-    traffic = _traffic_summary()
+    traffic = None if ragged else _traffic_summary()  # the committed capture is of the kimi_k2 workload
     clk = clocks.summary()
     if rank != 0:
         return None
-    cpu = cpu_baseline_sample(args.cpu_baseline_seconds) if (world == 1 and args.cpu_baseline_seconds > 0) else None
+    cpu = cpu_baseline_sample(args.cpu_baseline_seconds) if (world == 1 and args.cpu_baseline_seconds > 0
+                                                                 and not ragged) else None
     line = {
         "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "us_per_layer": round(ms_step * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong" if ragged else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded normal q and latents, cache written by the library's MXFP4 KV-append)",
-        "config": {"workload": WORKLOAD, "heads": HEADS, "batch_per_gpu": BATCH, "ctx": CTX, "page_size": PAGE,
-                   "num_kv_splits": f"auto (balanced schedule over {splits} CTAs)", "sm_scale": "1/sqrt(192)",
-                   "algorithmic_bytes_per_gpu_step": nbytes,
-                   "l2": "inputs larger than L2: two independent 210 MB caches alternated between steps",
-                   "parallelism": f"dp{world} (batch-sharded, no collective in the step)"},
+        "config": ({"workload": RAGGED_WORKLOAD, "heads": HEADS, "batch_total": RAGGED_BATCH,
+                    "batch_this_rank": wl[0]["batch"], "tokens_total": sum(wl[0]["lens"]), "page_size": PAGE,
+                    "num_kv_splits": f"auto (balanced schedule over {splits} CTAs)", "sm_scale": "1/sqrt(192)",
+                    "algorithmic_bytes_per_job_step": nbytes_job,
+                    "l2": "inputs larger than L2: one ~1.7 GB / N cache per rank",
+                    "parallelism": f"dp{world} (sequences bin-packed over ranks; outputs gathered to rank 0 "
+                                   "outside the timed steps)",
+                    "gather_ms": None if gather_ms is None else round(gather_ms, 5)}
+                   if ragged else
+                   {"workload": WORKLOAD, "heads": HEADS, "batch_per_gpu": BATCH, "ctx": CTX, "page_size": PAGE,
+                    "num_kv_splits": f"auto (balanced schedule over {splits} CTAs)", "sm_scale": "1/sqrt(192)",
+                    "algorithmic_bytes_per_gpu_step": nbytes,
+                    "l2": "inputs larger than L2: two independent 210 MB caches alternated between steps",
+                    "parallelism": f"dp{world} (batch-sharded, no collective in the step)"}),
         "e2e": {"value": round(e2e_tbs, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms / args.steps, 5),
                 "path": "kimi_b200.mla_decode_fwd with q + page table copied from pinned host memory and o "
@@ -354,6 +441,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["kimi_k2", "ragged"], default="kimi_k2")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
                     help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
     args = ap.parse_args()

@@ -101,3 +101,26 @@ def test_partial_then_merge_equals_one_call(splits):
                                workspace=ws)
     torch.cuda.synchronize()
     assert torch.equal(o1, o2)
+
+
+def test_batch_sharded_ranks_on_one_gpu_match_the_oracle():
+    # the data-parallel path with its ranks run one after another on this GPU:
+    # each decodes its bin-packed share through its own page table, the shares
+    # are put back in batch order (as kimi_b200.dp.gather_outputs does on rank 0)
+    from kimi_b200 import dp
+    from tests.test_gpu_parity import _gpu_inputs
+    rng = np.random.default_rng(15)
+    lens = [int(x) for x in rng.integers(1, 3000, 24)] + [0]
+    case = make_case(lens, 64, seed=15)
+    q, kvb, kvs, ip, ix, last = _gpu_inputs(case)
+    world = 3
+    shards = dp.shard_sequences(lens, world)
+    out = torch.full((len(lens), 64, 512), float("nan"), dtype=torch.bfloat16, device="cuda:0")
+    for r in range(world):
+        lip, lix, llast = dp.local_batch(shards[r], ip, ix, last)
+        o_local = torch.empty(len(shards[r]), 64, 512, dtype=torch.bfloat16, device="cuda:0")
+        kimi_b200.mla_decode_fwd(q[shards[r]].contiguous(), kvb, kvs, o_local, None, lip, lix, llast,
+                                 sm_scale=case["sm_scale"])
+        out[torch.tensor(shards[r], dtype=torch.long, device="cuda:0")] = o_local
+    torch.cuda.synchronize()
+    _check(case, out.float().cpu().numpy())

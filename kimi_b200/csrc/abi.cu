@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/kimi_mla.h"
@@ -33,15 +34,90 @@ int device_sm_count() {
   return cached[dev];
 }
 
-// KIMI_MLA_DECODE_KERNEL=mma selects the warp-level mma.sync decode (kept for
-// comparison); the default is the tcgen05 kernel.
-bool use_warp_mma_kernel() {
+// Stage-1 kernel: the block-scaled fp4 tensor-core kernel by default;
+// KIMI_MLA_DECODE_KERNEL=tc selects the fp8-dequantising tcgen05 kernel and
+// =mma the warp-level mma.sync kernel (both kept for comparison).
+enum class Stage1 { kFp4, kTc, kMma };
+
+Stage1 stage1_kernel() {
   static int choice = -1;
   if (choice < 0) {
     const char* v = std::getenv("KIMI_MLA_DECODE_KERNEL");
-    choice = (v && std::strcmp(v, "mma") == 0) ? 1 : 0;
+    choice = (v && std::strcmp(v, "mma") == 0) ? 2 : (v && std::strcmp(v, "tc") == 0) ? 1 : 0;
   }
-  return choice == 1;
+  return choice == 2 ? Stage1::kMma : choice == 1 ? Stage1::kTc : Stage1::kFp4;
+}
+
+bool use_warp_mma_kernel() { return stage1_kernel() == Stage1::kMma; }
+
+// cuTensorMapEncodeTiled, from the driver through the runtime (no link
+// against libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// TMA maps of the paged cache for the fp4 kernel: kv_buffer as a
+// [num_pages * 64, 384] byte matrix read in boxes of 128 bytes x 64 rows
+// (128-byte swizzle: the MMA operand layout), kv_scales as [num_pages * 64,
+// 16] in boxes of 16 x 64.  Reads past either end yield zeros.  The last
+// encoding is kept (it depends only on the two base pointers and the page
+// count).
+bool encode_cache_maps(const void* kv_buffer, const void* kv_scales, int64_t num_pages, CUtensorMap& kv_map,
+                       CUtensorMap& sc_map) {
+  struct Last {
+    const void* kv = nullptr;
+    const void* sc = nullptr;
+    int64_t pages = -1;
+    CUtensorMap kv_map, sc_map;
+  };
+  static thread_local Last last;
+  if (last.kv == kv_buffer && last.sc == kv_scales && last.pages == num_pages) {
+    kv_map = last.kv_map;
+    sc_map = last.sc_map;
+    return true;
+  }
+  const EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  const cuuint64_t rows = static_cast<cuuint64_t>(num_pages > 0 ? num_pages : 1) * kimi::kPageSize;
+  const cuuint32_t unit[2] = {1, 1};
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kimi::kTokenBytes), rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kimi::kTokenBytes)};
+    const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(kimi::kPageSize)};
+    if (enc(&kv_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(kv_buffer), dims, strides, box, unit,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kimi::kScaleBytes), rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kimi::kScaleBytes)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kimi::kScaleBytes), static_cast<cuuint32_t>(kimi::kPageSize)};
+    if (enc(&sc_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(kv_scales), dims, strides, box, unit,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  last.kv = kv_buffer;
+  last.sc = kv_scales;
+  last.pages = num_pages;
+  last.kv_map = kv_map;
+  last.sc_map = sc_map;
+  return true;
 }
 
 // How one call is laid out on the GPU.
@@ -133,6 +209,7 @@ namespace {
 struct Prepared {
   Plan plan;
   kimi::DecodeArgs args;
+  kimi::CacheMaps maps;  // fp4 kernel only
 };
 
 int prepare(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, Prepared& out) {
@@ -179,12 +256,19 @@ int prepare(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_byte
   a.balanced = plan.balanced ? 1 : 0;
   a.sm_scale = p->sm_scale;
   a.status = nullptr;
+  if (stage1_kernel() == Stage1::kFp4 &&
+      !encode_cache_maps(p->kv_buffer, p->kv_scales, p->num_pages, out.maps.kv, out.maps.sc))
+    return KIMI_ERR_UNSUPPORTED;
   out.plan = plan;
   return KIMI_OK;
 }
 
 int launch_stage1(const Prepared& pr, cudaStream_t s) {
-  return cuda_status(use_warp_mma_kernel() ? kimi::launch_decode_mma(pr.args, s) : kimi::launch_decode_tc(pr.args, s));
+  switch (stage1_kernel()) {
+    case Stage1::kMma: return cuda_status(kimi::launch_decode_mma(pr.args, s));
+    case Stage1::kTc: return cuda_status(kimi::launch_decode_tc(pr.args, s));
+    default: return cuda_status(kimi::launch_decode_fp4(pr.args, pr.maps, s));
+  }
 }
 
 int launch_merge(const Prepared& pr, cudaStream_t s) {

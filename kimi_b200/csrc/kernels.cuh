@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -79,6 +80,14 @@ struct DecodeArgs {
   float sm_scale;
 };
 
+// TMA maps of the cache for the fp4 tensor-core kernel: kv_buffer as a
+// [num_pages * 64, 384] byte matrix (box 128 x 64 rows, 128-byte swizzle) and
+// kv_scales as [num_pages * 64, 16] (box 16 x 64 rows).
+struct CacheMaps {
+  CUtensorMap kv;
+  CUtensorMap sc;
+};
+
 struct ReduceArgs {
   const void* partial_o;      // [slots, heads, 512], bf16 (this library's decode) or fp32
   int partial_bf16;
@@ -97,6 +106,7 @@ cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream);
+cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream);
 cudaError_t launch_reduce(const ReduceArgs& a, cudaStream_t stream);
 
 }  // namespace kimi

@@ -1,0 +1,904 @@
+// Split-K absorbed-MLA decode over the MXFP4 paged cache, sm_100a: Q K^T as
+// block-scaled e2m1 tensor-core MMAs straight from the cache bytes.
+//
+// Math (paths inside ianye23301/kimi): the archive stage-1 kernel
+// `_mla_decode_split_kv` (archive/mla-mxfp4-dead-end/mla_decode_mxfp4_v5.py:136-261),
+// which likewise computes Q K^T with an MXFP4 x MXFP4 block-scaled dot
+// (`tl.dot_scaled(q_fp4, q_scale, "e2m1", k_u8, k_scale, "e2m1")`), under the
+// contract of `reference_mla_decode` (tests/test_triton_mla_decode.py:12-62):
+//   S = q_nope . k_nope + q_pe . k_pe,  P = softmax(S * sm_scale),  O = P . k_nope.
+//
+// Scheduling is that of the other tensor-core kernel (decode_common.cuh): one
+// CTA = up to 64 heads over a run of 128-token tiles (two pages), tokens on
+// the MMA's M dimension and heads on N.
+//   * Q K^T: the tile's nibbles and e8m0 scales are loaded by TMA as they lie
+//     in the cache (nibbles as two 128-byte-swizzled K-major column blocks of
+//     128 rows; scales row by row) and consumed by tcgen05.mma kind::mxf4 with
+//     the scales in TMEM.  q_nope is written as three block-scaled e2m1 terms
+//     (q = t0 + t1 + t2, each term the e2m1 rounding of the remaining residual
+//     with its own e8m0 scale per 32 elements), stacked as one N = 192 B
+//     operand; the terms land in S column groups 0, 64 and 128 and are summed
+//     by the softmax.  Three terms give bf16-level scores; the reference
+//     quantises q to a single e2m1 term.  q_pe . k_pe is a bf16 MMA with k_pe
+//     (TMA-loaded) and q_pe in shared memory, accumulated into column group 0.
+//   * P V: P'' = exp2(x - R_h) as two e4m3 terms (hi + residual) against
+//     V'' = e2m1 * 2^(scale - 127 - sigma) written as e5m2 (exact) by the
+//     loader warps from the TMA-loaded nibbles; two PV MMAs per K step into
+//     one accumulator (one e4m3 term alone costs ~2% relative error on short
+//     contexts).  R_h (per-head offset, kept in [max - 8.5, max - 4] of the
+//     running max) and sigma (per-tile reference exponent) are raised lazily;
+//     O is rescaled in TMEM when either changes.
+//   * Shared memory (228 KB): two stages of raw nibbles + scales, one k_pe
+//     buffer, a two-slot V'' ring by latent half (the loaders fill half h of
+//     tile j as soon as PV has finished half h of tile j - 1), Q, q_pe and P''.
+//   * TMEM (512 columns): S [0,192), scale factors of A (two buffers, 16
+//     columns each) [192,224), of B [224,256), O^T [256,512) as four 128-row
+//     latent chunks of 64 head columns.
+//
+// Warp roles (20 warps, 640 threads):
+//   warps 0-7   softmax: Q terms of each piece, S(j) -> P''(j), O rescales,
+//               the epilogue;
+//   warps 8-15  loaders: tile maximum scale (sigma), A scale factors to TMEM
+//               (warps 8-11, one per TMEM lane quarter), V'' halves;
+//   warp 16     allocates TMEM and issues QK(j) (RoPE MMAs first);
+//   warps 17-18 issue PV(j), latent half 0 and half 1;
+//   warp 19     TMA producer: nibbles + scales two tiles ahead, k_pe one tile
+//               ahead, L2 prefetch further ahead.
+// Every mbarrier wait is bounded; a wait that gives up sets a shared abort
+// word that every other wait polls, each role leaves its loop, the issuers
+// drain their MMAs and TMEM is freed as usual.
+#include <cstddef>
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include "decode_common.cuh"
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+namespace kimi {
+namespace {
+
+using namespace sm100;
+using namespace dec;
+
+constexpr int kNH = 64;  // heads per CTA
+constexpr int kSoftmaxWarps = 8;
+constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
+constexpr int kLoaderWarp0 = 8;  // warps 8..15
+constexpr int kLoaderWarps = 8;
+constexpr int kLoaderThreads = 32 * kLoaderWarps;
+constexpr int kWarpQK = 16;
+constexpr int kWarpPV0 = 17;  // warps 17, 18
+constexpr int kWarpTMA = 19;
+constexpr int kThreads = 640;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColSfa = 192, kColSfb = 224, kColO = 256;
+constexpr uint32_t kPollLimit = 100000;  // polls of up to kWaitSleepNs each: about 2 s
+constexpr int kPrefetchTiles = 4;        // L2 prefetch distance beyond the TMA loads
+
+// Register budgets: 640 threads launch with 96 registers each (61440); the
+// softmax warpgroups take 128, the loaders give back down to 80, the
+// issuer/producer warpgroup to 56.
+constexpr uint32_t kLaunchRegs = 96;
+constexpr uint32_t kSoftmaxRegs = 128, kLoaderRegs = 80, kIssuerRegs = 56;
+static_assert(kSoftmaxThreads * kSoftmaxRegs + kLoaderThreads * kLoaderRegs + 128 * kIssuerRegs <=
+                  kThreads * kLaunchRegs,
+              "register split");
+
+// Named barriers (0 is __syncthreads)
+constexpr int kBarSoftmax = 1;
+constexpr int kBarLoader = 2;
+
+// Shared memory (bytes).  Swizzled operands use 128B-swizzled atoms of 8 rows
+// x 128 bytes (1 KB), rows of a column block 128 bytes apart.
+constexpr int kNibBlock = 128 * 128;        // 128 token rows x 128 nibble bytes (K 0..255 or 256..511)
+constexpr int kNibStage = 2 * kNibBlock;    // one tile's nibbles
+constexpr int kOffNib = 0;                  // two stages
+constexpr int kScStage = 128 * kScaleBytes; // one tile's e8m0 scales, token-major
+constexpr int kScSlots = 4;                 // scale ring: tiles j .. j + 3
+constexpr int kOffSc = kOffNib + 2 * kNibStage;
+constexpr int kOffKpe = kOffSc + kScSlots * kScStage;  // k_pe: 128 rows x 128 bytes
+constexpr int kVCol = 16384;                // V'': one 128-latent column (16 atoms of 8 tokens)
+constexpr int kOffV = kOffKpe + 128 * 128;  // one tile, four latent columns; ring of 4 token quarters
+constexpr int kQBlock = 192 * 128;          // Q terms: 192 rows x 128 bytes per K column block
+constexpr int kOffQ = kOffV + 4 * kVCol;
+constexpr int kOffQpe = kOffQ + 2 * kQBlock;  // q_pe bf16: 64 rows x 128 bytes
+constexpr int kOffP = kOffQpe + 64 * 128;     // P'' hi e4m3, MN-major cores (token group 0..15, head bytes 0..3)
+constexpr int kOffPlo = kOffP + 8192;         // P'' lo (residual), same layout
+constexpr int kPRow = 4 * 128;
+constexpr int kOffMisc = kOffPlo + 8192;
+static_assert(kOffKpe % 1024 == 0 && kOffV % 1024 == 0 && kOffQ % 1024 == 0 && kOffQpe % 1024 == 0 &&
+                  kOffP % 1024 == 0,
+              "swizzled operands start on 1 KB boundaries");
+
+struct Misc {
+  uint64_t mb_rawfull[2];    // nibble stage s landed (producer expect_tx + TMA bytes)
+  uint64_t mb_qkdone[2];     // stage s: QK of its tile complete (commit)
+  uint64_t mb_nibread[2];    // stage s: the loader warps are done with its tile (8 arrivals)
+  uint64_t mb_scfull[4];     // scale ring slot r landed (producer expect_tx + TMA bytes)
+  uint64_t mb_sfafull[2];    // A scale-factor buffer s written (4 loader warps)
+  uint64_t mb_vfull[4];      // V'' token quarter k of the current tile written (8 loader warps)
+  uint64_t mb_pvq[4];        // PV of token quarter k complete (one commit per PV issuer)
+  uint64_t mb_sigready[4];   // sigma of tile j published in sig[j % 4] (1 arrival)
+  uint64_t mb_kpefull;       // k_pe of the next tile landed
+  uint64_t mb_kpefree;       // RoPE MMAs of the tile in the k_pe buffer complete (commit)
+  uint64_t mb_sfull;         // QK(j) complete (commit)
+  uint64_t mb_sfree;         // S(j) read out of TMEM (8 softmax warps)
+  uint64_t mb_pfull;         // P''(j) written, O rescaled (8 softmax warps)
+  uint64_t mb_qready;        // Q terms, their scales and q_pe of a piece written (8 softmax warps)
+  uint64_t mb_drain;         // each issuer's last commit (3 arrivals)
+  SchedScratch sched;        // balanced mode: block-scan scratch
+  uint32_t tmem_base;
+  int abort_flag;
+  int tile_smax[4];          // max e8m0 byte of tile j in slot j % 4 (reset two tiles ahead)
+  int sig[4];                // reference exponent sigma of tile j in slot j % 4
+  alignas(16) float R[kNH];  // per-head exp2 offset, log2 units (read as float4)
+  float alpha[kNH];          // O rescale factors of the current event
+  float beta[kNH];           // softmax-sum rescale factors of the current event
+  float red[4][kNH];         // cross-warp reduction scratch
+};
+constexpr int kSmem = kOffMisc + static_cast<int>(sizeof(Misc));
+static_assert(kSmem <= 232448, "shared memory budget");
+static_assert(kOffMisc % 16 == 0 && offsetof(Misc, R) % 16 == 0, "per-head arrays are read with 16-byte loads");
+static_assert(kOffP + 192 * kScaleBytes <= kOffMisc, "Q scale staging fits in P''");
+
+__device__ __forceinline__ uint8_t* smem_base() {
+  extern __shared__ __align__(1024) uint8_t dyn_smem[];
+  return dyn_smem;
+}
+
+__device__ __forceinline__ void record_status(const DecodeArgs& a, int bits) {
+  if (a.status) atomicOr(a.status, bits);
+}
+
+// Per-thread bounded wait; on give-up records the failure and raises the abort word.
+__device__ __forceinline__ bool wait_phase(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit) {
+  if (mbar_wait_or_abort(mb, parity, kPollLimit, &ms.abort_flag)) return true;
+  if (atomicExch(&ms.abort_flag, 1) == 0) record_status(a, bit);
+  return false;
+}
+
+// Warp-uniform bounded wait: lane 0 polls, the warp gets its verdict.
+__device__ __forceinline__ bool warp_wait(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit,
+                                          int lane) {
+  bool ok = true;
+  if (lane == 0) ok = wait_phase(mb, parity, ms, a, bit);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// Page rows (y coordinates of the cache tensor maps) of the two pages of the
+// cursor's tile: -1 for a slot past the sequence's pages (nothing loaded);
+// an out-of-range page id maps to a row outside the tensor, which TMA fills
+// with zeros.
+__device__ __forceinline__ void tile_rows(const DecodeArgs& a, const Cursor& c, int (&y)[2]) {
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    const int p = 2 * c.tile + slot;
+    const bool in_range = p < c.n_pages;
+    const int pid = ldg_s32_or(a.kv_indices + c.page_lo + (in_range ? p : 0), in_range, -1);
+    y[slot] = !in_range ? -1 : (pid >= 0 && pid < a.num_pages) ? pid * kPageSize : -kPageSize;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA producer (warp 19, lane 0)
+// ---------------------------------------------------------------------------
+// Nibbles go to a two-stage ring (tile j waits for QK(j - 2) and the loaders'
+// V'' of tile j - 2), scales to a four-slot ring two tiles ahead of the
+// nibbles (the loaders need tile j + 1's scales while converting tile j), k_pe
+// to one buffer (tile j waits for the RoPE MMAs of tile j - 1).
+__device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArgs& a, const CacheMaps& maps) {
+  prefetch_tensormap(&maps.kv);
+  prefetch_tensormap(&maps.sc);
+  Cursor cur, sc_cur, pc;  // nibbles and k_pe of tile j; the next tile's scales; L2 prefetch
+  cursor_start(a, sc, cur);
+  sc_cur = cur;
+  int sc_issued = 0;
+  auto load_scales = [&]() {  // tile sc_issued -> ring slot sc_issued % 4
+    int y[2];
+    tile_rows(a, sc_cur, y);
+    uint64_t* mb = &ms.mb_scfull[sc_issued % kScSlots];
+    const int slots = (y[0] != -1 ? 1 : 0) + (y[1] != -1 ? 1 : 0);
+    mbar_arrive_expect_tx(mb, static_cast<uint32_t>(slots * kPageScaleBytes));
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot)
+      if (y[slot] != -1)
+        tma_load_2d(sm + kOffSc + (sc_issued % kScSlots) * kScStage + slot * kPageScaleBytes, &maps.sc, 0, y[slot], mb);
+    ++sc_issued;
+    cursor_next(a, sc_cur);
+  };
+  // L2 prefetch of the tiles the TMA loads reach later (tiles 0 and 1 are loaded at once)
+  pc = cur;
+  cursor_next(a, pc);
+  cursor_next(a, pc);
+  int prefetched = 2;
+  auto prefetch_upto = [&](int upto) {
+    while (prefetched < min(upto, sc.count)) {
+      int y[2];
+      tile_rows(a, pc, y);
+#pragma unroll
+      for (int slot = 0; slot < 2; ++slot) {
+        if (y[slot] >= 0) {
+          prefetch_l2(a.kv_buffer + static_cast<int64_t>(y[slot]) * kTokenBytes, kPageBytes);
+          prefetch_l2(a.kv_scales + static_cast<int64_t>(y[slot]) * kScaleBytes, kPageScaleBytes);
+        }
+      }
+      ++prefetched;
+      cursor_next(a, pc);
+    }
+  };
+  for (int t = 0; t < min(2, sc.count); ++t) load_scales();
+  prefetch_upto(2 + kPrefetchTiles);
+  int issued = 0;
+  for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
+    const int s = j & 1;
+    // stage s (and scale slot (j + 2) % 4) were last used by tile j - 2
+    if (j >= 2) {
+      const uint32_t par = static_cast<uint32_t>(((j - 2) >> 1) & 1);
+      if (!wait_phase(&ms.mb_qkdone[s], par, ms, a, 256) || !wait_phase(&ms.mb_nibread[s], par, ms, a, 256)) break;
+    }
+    if (j + 2 < sc.count) load_scales();
+    int y[2];
+    tile_rows(a, cur, y);
+    const int slots = (y[0] != -1 ? 1 : 0) + (y[1] != -1 ? 1 : 0);
+    mbar_arrive_expect_tx(&ms.mb_rawfull[s], static_cast<uint32_t>(slots * 2 * 64 * 128));
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot) {
+      if (y[slot] == -1) continue;
+      uint8_t* nib = sm + kOffNib + s * kNibStage + slot * (64 * 128);
+      tma_load_2d(nib, &maps.kv, 0, y[slot], &ms.mb_rawfull[s]);
+      tma_load_2d(nib + kNibBlock, &maps.kv, 128, y[slot], &ms.mb_rawfull[s]);
+    }
+    // k_pe (one buffer): free once the RoPE MMAs of tile j - 1 are complete
+    if (j >= 1 && !wait_phase(&ms.mb_kpefree, static_cast<uint32_t>((j - 1) & 1), ms, a, 256)) break;
+    mbar_arrive_expect_tx(&ms.mb_kpefull, static_cast<uint32_t>(slots * 64 * 128));
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot) {
+      if (y[slot] == -1) continue;
+      tma_load_2d(sm + kOffKpe + slot * (64 * 128), &maps.kv, kNibbleBytes, y[slot], &ms.mb_kpefull);
+    }
+    issued = j + 1;
+    prefetch_upto(j + 3 + kPrefetchTiles);
+  }
+  // every load issued has landed before the CTA may exit (normally the
+  // consumers have already waited for all of them)
+  for (int j = max(0, issued - 2); j < issued; ++j)
+    mbar_wait_bounded(&ms.mb_rawfull[j & 1], static_cast<uint32_t>((j >> 1) & 1), kPollLimit);
+  if (issued > 0) mbar_wait_bounded(&ms.mb_kpefull, static_cast<uint32_t>((issued - 1) & 1), kPollLimit);
+  for (int t = max(0, sc_issued - kScSlots); t < sc_issued; ++t)
+    mbar_wait_bounded(&ms.mb_scfull[t % kScSlots], static_cast<uint32_t>((t / kScSlots) & 1), kPollLimit);
+}
+
+// ---------------------------------------------------------------------------
+// Issuers (warp 16: QK, warps 17-18: PV; lane 0 issues)
+// ---------------------------------------------------------------------------
+__device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int lane, const DecodeArgs& a) {
+  const uint32_t id_pe = instr_desc(kFmtBF16, kFmtBF16, false, false, 128, 64);
+  const uint32_t sQ = smem_addr(sm + kOffQ), sQpe = smem_addr(sm + kOffQpe), sKpe = smem_addr(sm + kOffKpe);
+  Cursor cur;
+  cursor_start(a, sc, cur);
+  int pieces = 0;
+  for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
+    const int s = j & 1;
+    const uint32_t use = static_cast<uint32_t>((j >> 1) & 1);
+    // QK(j) needs the tile's nibbles/scales, its k_pe and A scale factors, S(j-1)
+    // read out of TMEM (single S buffer), and at a piece start that sequence's Q.
+    if (!warp_wait(&ms.mb_rawfull[s], use, ms, a, 16, lane) ||
+        !warp_wait(&ms.mb_kpefull, static_cast<uint32_t>(j & 1), ms, a, 16, lane) ||
+        !warp_wait(&ms.mb_sfafull[s], use, ms, a, 16, lane))
+      break;
+    if (j > 0 && !warp_wait(&ms.mb_sfree, static_cast<uint32_t>((j - 1) & 1), ms, a, 16, lane)) break;
+    if (cursor_first(cur)) {
+      if (!warp_wait(&ms.mb_qready, static_cast<uint32_t>(pieces & 1), ms, a, 16, lane)) break;
+      ++pieces;
+    }
+    fence_after_sync();
+    if (lane == 0) {
+      // RoPE first (k_pe is single-buffered): S[:, 0:64) = k_pe . q_pe^T
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma_f16_ss(tmem + kColS, smem_desc(sKpe + 32 * k, 16, 1024, kSwizzle128B),
+                   smem_desc(sQpe + 32 * k, 16, 1024, kSwizzle128B), id_pe, k > 0 ? 1u : 0u);
+      mma_commit(&ms.mb_kpefree);
+      // latent: 8 K steps of 64; the first adds onto the RoPE columns (term 0)
+      // and starts the columns of terms 1 and 2
+      const uint32_t sA = smem_addr(sm + kOffNib + s * kNibStage);
+      const uint32_t sfa0 = tmem + kColSfa + 16 * s, sfb0 = tmem + kColSfb;
+#pragma unroll 1
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t koff = (k & 3) * 32;
+        const uint32_t byte = 2 * (k & 1);
+        const uint32_t sfa = (sfa0 + 4 * (k >> 1)) | (byte << 30);
+        const uint32_t sfb = (sfb0 + 8 * (k >> 1)) | (byte << 30);
+        const uint64_t da = smem_desc(sA + (k >> 2) * kNibBlock + koff, 16, 1024, kSwizzle128B);
+        const uint32_t qb = sQ + (k >> 2) * kQBlock + koff;
+        if (k == 0) {
+          mma_mxf4_ss(tmem + kColS, da, smem_desc(qb, 16, 1024, kSwizzle128B), instr_desc_mxf4(64, byte, byte),
+                      sfa, sfb, 1u);
+          mma_mxf4_ss(tmem + kColS + 64, da, smem_desc(qb + 8 * 1024, 16, 1024, kSwizzle128B),
+                      instr_desc_mxf4(128, byte, byte), sfa, (sfb0 + 2) | (byte << 30), 0u);
+        } else {
+          mma_mxf4_ss(tmem + kColS, da, smem_desc(qb, 16, 1024, kSwizzle128B), instr_desc_mxf4(192, byte, byte),
+                      sfa, sfb, 1u);
+        }
+      }
+      mma_commit(&ms.mb_sfull);
+      mma_commit(&ms.mb_qkdone[s]);
+    }
+    __syncwarp();
+  }
+}
+
+// PV issuer h owns latent half h (chunks 2h, 2h + 1) and walks the tile's
+// four token quarters as the loaders finish them.
+__device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int lane, int h,
+                          const DecodeArgs& a) {
+  const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, 64);
+  const uint32_t sP = smem_addr(sm + kOffP), sPlo = smem_addr(sm + kOffPlo);
+  const uint32_t sV = smem_addr(sm + kOffV + 2 * h * kVCol);
+  Cursor cur;
+  cursor_start(a, sc, cur);
+  for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
+    const uint32_t par = static_cast<uint32_t>(j & 1);
+    if (!warp_wait(&ms.mb_pfull, par, ms, a, 32, lane)) break;
+    const bool fresh = cursor_first(cur);  // the piece's first PV starts the accumulator
+    bool ok = true;
+#pragma unroll 1
+    for (int k = 0; k < 4 && ok; ++k) {
+      ok = warp_wait(&ms.mb_vfull[k], par, ms, a, 32, lane);
+      if (!ok) break;
+      fence_after_sync();
+      if (lane == 0) {
+        const uint64_t phi = smem_desc(sP + k * 4 * kPRow, kPRow, 128);
+        const uint64_t plo = smem_desc(sPlo + k * 4 * kPRow, kPRow, 128);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          mma_f8f6f4_ss(tmem + kColO + 64 * (2 * h + c),
+                        smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B), phi, id_pv,
+                        (fresh && k == 0) ? 0u : 1u);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          mma_f8f6f4_ss(tmem + kColO + 64 * (2 * h + c),
+                        smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B), plo, id_pv, 1u);
+        mma_commit(&ms.mb_pvq[k]);
+      }
+      __syncwarp();
+    }
+    if (!ok) break;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Loaders (warps 8..15)
+// ---------------------------------------------------------------------------
+// Per tile j: first the reference exponent sigma and the A scale factors of
+// tile j + 1 (QK(j + 1) needs them while PV(j) still runs), then V''(j) one
+// token quarter at a time, each as soon as PV(j - 1) has finished reading that
+// quarter of the ring.
+__device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int warp, int lane,
+                       const DecodeArgs& a) {
+  const int lt = threadIdx.x - 32 * kLoaderWarp0;  // 0..255
+  const int lw = lt >> 5;
+  const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+  int prev_sigma = 0;
+  // sigma and A scale factors of tile tt (cursor c); false when the CTA aborts
+  auto scales = [&](int tt, const Cursor& c) -> bool {
+    const int r = tt % kScSlots;
+    const uint8_t* scb = sm + kOffSc + r * kScStage;
+    const bool ok = warp_wait(&ms.mb_scfull[r], static_cast<uint32_t>((tt / kScSlots) & 1), ms, a, 64, lane);
+    const int nvalid = cursor_valid(c);
+    // tile maximum of the e8m0 bytes of valid tokens -> reference exponent
+    uint32_t my_max = 0u;
+    if (ok && (lt >> 1) < nvalid) {
+      const uint2 w = *reinterpret_cast<const uint2*>(scb + (lt >> 1) * kScaleBytes + 8 * (lt & 1));
+      const uint32_t m4 = __vmaxu4(w.x, w.y);
+      my_max = max(max(m4 & 0xFFu, (m4 >> 8) & 0xFFu), max((m4 >> 16) & 0xFFu, m4 >> 24));
+    }
+    my_max = __reduce_max_sync(0xffffffffu, my_max);
+    if (lane == 0) atomicMax(&ms.tile_smax[tt & 3], static_cast<int>(my_max));
+    if (bar_or(kBarLoader, kLoaderThreads, !ok)) return false;
+    const int smax = ms.tile_smax[tt & 3];
+    int sigma;
+    if (cursor_first(c)) {
+      sigma = smax - 127 - 8;  // tile max maps to <= 6 * 2^8 in V''
+    } else {
+      const int kmax = smax - 127 - prev_sigma;
+      sigma = (kmax > 13 || kmax < -4) ? smax - 127 - 8 : prev_sigma;
+    }
+    prev_sigma = sigma;
+    if (lt == 0) {
+      ms.tile_smax[(tt + 2) & 3] = 0;
+      ms.sig[tt & 3] = sigma;
+      mbar_arrive(&ms.mb_sigready[tt & 3]);
+    }
+    // A scale factors -> TMEM buffer tt % 2 (last read by QK(tt - 2)); warp
+    // 8 + q writes TMEM lane quarter q: column 4 k4 + r1 of lane r0 holds the
+    // scale word k4 of token r0 + 32 r1.
+    if (lw < 4) {
+      const int s = tt & 1;
+      const bool free_ok =
+          tt < 2 || warp_wait(&ms.mb_qkdone[s], static_cast<uint32_t>(((tt - 2) >> 1) & 1), ms, a, 64, lane);
+      if (free_ok) {
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          v[i] = *reinterpret_cast<const uint32_t*>(scb + (lane + 32 * (i & 3)) * kScaleBytes + 4 * (i >> 2));
+        tmem_st16(tmem + lane_base + kColSfa + 16 * s, v);
+        tmem_st_wait();
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0 && free_ok) mbar_arrive(&ms.mb_sfafull[s]);
+    }
+    return true;
+  };
+
+  Cursor cur, nxt;  // tile j (V''), tile j + 1 (scales)
+  cursor_start(a, sc, cur);
+  nxt = cur;
+  if (!scales(0, nxt)) return;
+  int sigma = prev_sigma;  // of tile j
+  for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
+    if (j + 1 < sc.count) {
+      cursor_next(a, nxt);
+      if (!scales(j + 1, nxt)) break;
+    }
+    const int s = j & 1;
+    const uint8_t* nib = sm + kOffNib + s * kNibStage;
+    const uint8_t* scb = sm + kOffSc + (j % kScSlots) * kScStage;
+    const bool raw_ok = warp_wait(&ms.mb_rawfull[s], static_cast<uint32_t>((j >> 1) & 1), ms, a, 64, lane);
+    const int nvalid = cursor_valid(cur);
+    // V'' quarter k: warp lw converts tokens 32k + 4 lw .. + 3, lane l the
+    // 32-element group 8h + (l % 8) of token 32k + 4 lw + l / 8, h = 0, 1
+#pragma unroll 1
+    for (int k = 0; k < 4; ++k) {
+      const bool slot_ok =
+          raw_ok && (j == 0 || warp_wait(&ms.mb_pvq[k], static_cast<uint32_t>((j - 1) & 1), ms, a, 64, lane));
+      if (slot_ok) {
+        const int c = lane & 7;
+        const int t = 32 * k + 4 * lw + (lane >> 3);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint4 nb =
+              *reinterpret_cast<const uint4*>(nib + h * kNibBlock + (t >> 3) * 1024 + sw128_offset(t & 7, c));
+          const int sbyte = scb[t * kScaleBytes + 8 * h + c];
+          uint32_t lo, hi;
+          e5m2_tables(sbyte - 127 - sigma, lo, hi);
+          uint4 o0 = half_group_to_e5m2(nb.x, nb.y, lo, hi);
+          uint4 o1 = half_group_to_e5m2(nb.z, nb.w, lo, hi);
+          if (t >= nvalid) o0 = o1 = make_uint4(0u, 0u, 0u, 0u);
+          uint8_t* atom = sm + kOffV + (2 * h + (c >> 2)) * kVCol + (t >> 3) * 1024;
+          *reinterpret_cast<uint4*>(atom + sw128_offset(t & 7, 2 * (c & 3))) = o0;
+          *reinterpret_cast<uint4*>(atom + sw128_offset(t & 7, 2 * (c & 3) + 1)) = o1;
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0 && slot_ok) mbar_arrive(&ms.mb_vfull[k]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms.mb_nibread[s]);
+    sigma = prev_sigma;  // tile j + 1's, computed above
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Q of one sequence (softmax threads 0..255: 4 per head; part p handles the
+// 32-element blocks 4p .. 4p + 3 of the latent and 16-byte chunks 2p, 2p + 1 of q_pe)
+// ---------------------------------------------------------------------------
+__device__ void build_q(uint8_t* sm, Misc& ms, uint32_t tmem, const DecodeArgs& a, int b, int head_base,
+                        int heads_here, int warp, int lane) {
+  const int tid = threadIdx.x;
+  const int h = tid >> 2, part = tid & 3;
+  const bool live = h < heads_here;
+  const __nv_bfloat16* qrow = a.q + b * a.q_stride_b + (head_base + h) * a.q_stride_h;
+  uint8_t* sf_stage = sm + kOffP;  // [192 rows][16] e8m0 (P'' is free at a piece start)
+#pragma unroll 1
+  for (int blk = 0; blk < 4; ++blk) {
+    const int bl = 4 * part + blk;
+    float x[32];
+    {
+      uint4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        v[k] = live ? *reinterpret_cast<const uint4*>(qrow + 32 * bl + 8 * k) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t ws[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[8 * k + 2 * i] = __uint_as_float(ws[i] << 16);
+          x[8 * k + 2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+      // smallest e with amax <= 6 * 2^e: amax = 1.m * 2^f -> f - 2, or f - 1 when 1.m > 1.5
+      const uint32_t ab = __float_as_uint(amax);
+      int e = static_cast<int>(ab >> 23) - 129 + ((ab & 0x7FFFFFu) > 0x400000u ? 1 : 0);
+      e = max(-127, min(126, e));
+      const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+      const float scl = e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : __uint_as_float(0x00400000u);
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t byte = cvt_f32x2_e2m1x2(x[2 * i] * inv, x[2 * i + 1] * inv);
+        w[i >> 2] |= byte << (8 * (i & 3));
+        if (t < 2) {
+          const uint32_t h2 = cvt_e2m1x2_f16x2(byte);
+          x[2 * i] -= __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu))) * scl;
+          x[2 * i + 1] -= __half2float(__ushort_as_half(static_cast<unsigned short>(h2 >> 16))) * scl;
+        }
+      }
+      const int n = 64 * t + h;
+      *reinterpret_cast<uint4*>(sm + kOffQ + (bl >> 3) * kQBlock + (n >> 3) * 1024 + sw128_offset(n & 7, bl & 7)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+      sf_stage[n * kScaleBytes + bl] = static_cast<uint8_t>(e + 127);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int c = 2 * part + k;
+    const uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + kLatent + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(sm + kOffQpe + (h >> 3) * 1024 + sw128_offset(h & 7, c)) = v;
+  }
+  if (part == 0) ms.R[h] = 0.f;
+  named_bar(kBarSoftmax, kSoftmaxThreads);  // the scale bytes are staged
+  if (warp < 4) {
+    // B scale factors: column 8 k4 + n1 of lane n0 (every quarter alike) holds
+    // the scale word k4 of row n0 + 32 n1 (rows >= 192 are not read)
+    uint32_t u[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int n = lane + 32 * (i & 7);
+      u[i] = n < 192 ? *reinterpret_cast<const uint32_t*>(sf_stage + n * kScaleBytes + 4 * (i >> 3)) : 0x7F7F7F7Fu;
+    }
+    tmem_st32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + kColSfb, u);
+    tmem_st_wait();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Softmax warps (0..7) and the per-piece epilogue
+// ---------------------------------------------------------------------------
+__device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int head_base, int heads_here,
+                        int warp, int lane, float c_log2, const DecodeArgs& a) {
+  const int tid = threadIdx.x;
+  const int q = warp & 3;                  // TMEM lane quadrant
+  const int hf = warp >> 2;                // heads 32 hf .. 32 hf + 31
+  const int st = 32 * q + lane;            // softmax token
+  const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
+
+  float l_part[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
+  int sigma_prev = 0;
+  Cursor cur;
+  cursor_start(a, sc, cur);
+
+  for (int tile = 0; tile < sc.count; ++tile, cursor_next(a, cur)) {
+    const uint32_t par = static_cast<uint32_t>(tile & 1);
+    const bool first = cursor_first(cur);
+    if (first) {
+      // a new sequence: its Q replaces the previous one (whose last QK is
+      // complete: its S was read; its last PV too: the epilogue waited for it)
+      build_q(sm, ms, tmem, a, cur.b, head_base, heads_here, warp, lane);
+      fence_proxy_async_smem();
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ms.mb_qready);
+      named_bar(kBarSoftmax, kSoftmaxThreads);  // R of the new sequence is visible
+    }
+    bool ok = warp_wait(&ms.mb_sfull, par, ms, a, 1, lane);
+    fence_after_sync();
+    float t[32];
+    int sigma_cur = sigma_prev;
+    if (ok) {
+      {
+        uint32_t sv[32];
+        tmem_ld32(tmem + lane_base + kColS + 32 * hf, sv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(sv[j]);
+        tmem_ld32(tmem + lane_base + kColS + 64 + 32 * hf, sv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] += __uint_as_float(sv[j]);
+        tmem_ld32(tmem + lane_base + kColS + 128 + 32 * hf, sv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] += __uint_as_float(sv[j]);
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ms.mb_sfree);
+      ok = warp_wait(&ms.mb_sigready[tile & 3], static_cast<uint32_t>((tile >> 2) & 1), ms, a, 1, lane);
+      sigma_cur = ms.sig[tile & 3];
+      const bool tvalid = st < cursor_valid(cur);
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[32 * hf + j]);
+        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) t[j + u] = tvalid ? fmaf(t[j + u], c_log2, -rv[u]) : -CUDART_INF_F;
+      }
+      // PV(j-1) must be complete before O is rescaled or read, or P'' is overwritten
+      if (ok && tile > 0) {
+        const uint32_t pp = static_cast<uint32_t>((tile - 1) & 1);
+        ok = warp_wait(&ms.mb_pvq[3], pp, ms, a, 2, lane);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] = -CUDART_INF_F;
+    }
+    // rescale event: a piece's first tile, a score above R + 8.5, or a new sigma.
+    // One barrier ORs "event or failure"; only when it is raised does a second
+    // one tell a failure (leave the loop) from an event.
+    float tmaxv = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tmaxv = fmaxf(tmaxv, t[j]);
+    const bool need =
+        bar_or(kBarSoftmax, kSoftmaxThreads, !ok || first || tmaxv > 8.5f || sigma_cur != sigma_prev);
+    if (need && bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) break;
+    fence_after_sync();
+    if (need) {
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = t[j];
+      ms.red[q][32 * hf + lane] = warp_transpose_reduce<true>(v, lane);  // tile max of x - R_old
+      named_bar(kBarSoftmax, kSoftmaxThreads);
+      if (tid < kNH) {
+        const float tm = fmaxf(fmaxf(ms.red[0][tid], ms.red[1][tid]), fmaxf(ms.red[2][tid], ms.red[3][tid]));
+        // raise R so that this tile's max maps to 2^4 (only raise; a piece's first tile sets it)
+        const float shift = first ? tm - 4.0f : fmaxf(tm - 4.0f, 0.0f);
+        const float dshift = fmaxf(shift, -1e30f);
+        ms.R[tid] += dshift;
+        ms.beta[tid] = first ? 1.0f : ex2(-dshift);
+        ms.alpha[tid] = first ? 1.0f : ex2(-dshift + static_cast<float>(sigma_prev - sigma_cur));
+        ms.red[0][tid] = dshift;  // reused below as the per-head shift of t
+      }
+      named_bar(kBarSoftmax, kSoftmaxThreads);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] -= ms.red[0][32 * hf + j];
+      if (!first) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) l_part[j] *= ms.beta[32 * hf + j];
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * hf + cc;
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t vv[32];
+            const uint32_t ta = tmem + lane_base + kColO + 64 * c + 32 * hh;
+            tmem_ld32(ta, vv);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
+            tmem_st32(ta, vv);
+          }
+        }
+        tmem_st_wait();
+      }
+      // every thread has read red[0] and alpha before the next event overwrites them
+      named_bar(kBarSoftmax, kSoftmaxThreads);
+    }
+    sigma_prev = sigma_cur;
+
+    // ---- P'' = exp2(t) as e4m3 hi + residual, into the MN-major B operands ----
+    {
+      uint32_t pw[8], pl[8];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float p0 = ex2(t[j]);
+        const float p1 = ex2(t[j + 1]);
+        l_part[j] += p0;
+        l_part[j + 1] += p1;
+        uint16_t h8, l8;
+        split_e4m3x2(p0, p1, h8, l8);
+        if ((j & 2) == 0) {
+          pw[j / 4] = h8;
+          pl[j / 4] = l8;
+        } else {
+          pw[j / 4] |= static_cast<uint32_t>(h8) << 16;
+          pl[j / 4] |= static_cast<uint32_t>(l8) << 16;
+        }
+      }
+      const int prow = (st >> 3) * kPRow + (st & 7) * 16;
+      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf) * 128) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf + 1) * 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf) * 128) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf + 1) * 128) = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+    }
+    fence_proxy_async_smem();
+    fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ms.mb_pfull);
+
+    if (!cursor_last(cur)) continue;
+    // ---------------- epilogue of the piece ----------------
+    const bool done = warp_wait(&ms.mb_pvq[3], par, ms, a, 4, lane);
+    if (bar_or(kBarSoftmax, kSoftmaxThreads, !done)) break;
+    fence_after_sync();
+    {
+      const float s = warp_transpose_reduce<false>(l_part, lane);
+      ms.red[q][32 * hf + lane] = s;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
+    // the piece covers its whole sequence -> final output; otherwise a partial in its slot
+    const bool direct = a.balanced ? (cur.piece_begin == 0 && cur.piece_end == cursor_tiles(cur))
+                                   : a.num_splits == 1;
+    const int64_t slot = a.balanced ? static_cast<int64_t>(cur.b) + blockIdx.x
+                                    : static_cast<int64_t>(cur.b) * a.num_splits + blockIdx.x;
+    named_bar(kBarSoftmax, kSoftmaxThreads);
+    if (tid < kNH) {
+      const float l = ms.red[0][tid] + ms.red[1][tid] + ms.red[2][tid] + ms.red[3][tid];
+      // output factor 2^sigma / l per head (alpha is free again)
+      ms.alpha[tid] = l > 0.f ? exp2f(static_cast<float>(sigma_prev)) / l : 0.f;
+      if (!direct && tid < heads_here)
+        a.partial_lse[slot * a.num_heads + head_base + tid] = (ms.R[tid] + __log2f(l)) * kLn2;
+    }
+    if (a.balanced && tid == 0 && cur.piece_begin == 0) {
+      // this CTA holds the sequence's first tile: record its CTA span for the merge
+      const int last_cta = cta_of_tile(cur.seq_pos + cursor_tiles(cur) - 1, sc, gridDim.x);
+      a.seq_meta[cur.b] = make_int2(blockIdx.x, last_cta);
+    }
+    named_bar(kBarSoftmax, kSoftmaxThreads);
+    // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane
+#pragma unroll 1
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 2 * hf + cc;
+      const int d = 128 * c + 32 * q + lane;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t vv[32];
+        tmem_ld32(tmem + lane_base + kColO + 64 * c + 32 * hh, vv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int hd = 32 * hh + j;
+          if (hd < heads_here) {
+            const float val = __uint_as_float(vv[j]) * ms.alpha[hd];
+            const int hq = head_base + hd;
+            if (direct)
+              a.o[cur.b * a.o_stride_b + hq * a.o_stride_h + d] = __float2bfloat16_rn(val);
+            else
+              a.partial_o[(slot * a.num_heads + hq) * kLatent + d] = __float2bfloat16_rn(val);
+          }
+        }
+      }
+    }
+    // O and alpha are read before the next piece's PV / rescale touch them
+    fence_before_sync();
+    named_bar(kBarSoftmax, kSoftmaxThreads);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __grid_constant__ DecodeArgs a,
+                                                                  const __grid_constant__ CacheMaps maps) {
+  uint8_t* sm = smem_base();
+  Misc& ms = *reinterpret_cast<Misc*>(sm + kOffMisc);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int head_base = blockIdx.z * kNH;
+  const int heads_here = min(kNH, a.num_heads - head_base);
+
+  Sched sc;
+  if (a.balanced) {
+    balanced_schedule<kThreads>(a, ms.sched, sc);
+    if (sc.count == 0) {
+      // An empty run (fewer tiles than CTAs) can sit inside the CTA span of
+      // the sequence at its position; its slot of that sequence carries no weight.
+      if (sc.pos0 < sc.total && tid < heads_here)
+        a.partial_lse[(static_cast<int64_t>(sc.b0) + blockIdx.x) * a.num_heads + head_base + tid] = -CUDART_INF_F;
+      return;  // (uniform: every thread read the same count)
+    }
+  } else {
+    const int b = blockIdx.y, tiles = seq_tiles_of(a, b);
+    const int per_split = (tiles + a.num_splits - 1) / a.num_splits;
+    sc.b0 = b;
+    sc.off0 = blockIdx.x * per_split;
+    sc.count = max(0, min(per_split, tiles - sc.off0));
+    sc.pos0 = 0;
+    sc.total = 0;
+    sc.per_seq = sc.split_tiles = sc.seq_tiles = 0;
+    if (sc.count == 0) {
+      // nothing to attend to: zeros (one split) or a split that carries no weight
+      if (a.num_splits == 1) {
+        for (int i = tid; i < heads_here * (kLatent / 2); i += kThreads) {
+          const int h = i / (kLatent / 2), d = (i % (kLatent / 2)) * 2;
+          *reinterpret_cast<uint32_t*>(a.o + b * a.o_stride_b + (head_base + h) * a.o_stride_h + d) = 0u;
+        }
+      } else if (tid < heads_here) {
+        a.partial_lse[(static_cast<int64_t>(b) * a.num_splits + blockIdx.x) * a.num_heads + head_base + tid] =
+            -CUDART_INF_F;
+      }
+      return;
+    }
+  }
+
+  // ---------------- setup: barriers and TMEM ----------------
+  if (tid == 0) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ms.mb_rawfull[i], 1);
+      mbar_init(&ms.mb_qkdone[i], 1);
+      mbar_init(&ms.mb_nibread[i], kLoaderWarps);
+      mbar_init(&ms.mb_sfafull[i], 4);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&ms.mb_scfull[i], 1);
+      mbar_init(&ms.mb_vfull[i], kLoaderWarps);
+      mbar_init(&ms.mb_pvq[i], 2);
+      mbar_init(&ms.mb_sigready[i], 1);
+      ms.tile_smax[i] = 0;
+    }
+    mbar_init(&ms.mb_kpefull, 1);
+    mbar_init(&ms.mb_kpefree, 1);
+    mbar_init(&ms.mb_sfull, 1);
+    mbar_init(&ms.mb_sfree, kSoftmaxWarps);
+    mbar_init(&ms.mb_pfull, kSoftmaxWarps);
+    mbar_init(&ms.mb_qready, kSoftmaxWarps);
+    mbar_init(&ms.mb_drain, 3);
+    ms.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpQK) tmem_alloc(&ms.tmem_base, kTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = ms.tmem_base;
+
+  // Register budgets: the issuer and loader warpgroups give registers back
+  // before the softmax warpgroups' increase can be granted.
+  if (warp >= kWarpQK) {
+    setmaxnreg_dec<kIssuerRegs>();
+    if (warp == kWarpQK) {
+      qk_issuer(sm, ms, tmem, sc, lane, a);
+    } else if (warp < kWarpTMA) {
+      pv_issuer(sm, ms, tmem, sc, lane, warp - kWarpPV0, a);
+    } else if (lane == 0) {
+      producer(sm, ms, sc, a, maps);
+    }
+    // drain: arrives once every MMA this thread issued has completed
+    if (warp < kWarpTMA && lane == 0) mma_commit(&ms.mb_drain);
+    __syncwarp();
+  } else if (warp >= kLoaderWarp0) {
+    setmaxnreg_dec<kLoaderRegs>();
+    loader(sm, ms, tmem, sc, warp, lane, a);
+  } else {
+    setmaxnreg_inc<kSoftmaxRegs>();
+    softmax(sm, ms, tmem, sc, head_base, heads_here, warp, lane, a.sm_scale * kLog2e, a);
+  }
+
+  fence_before_sync();
+  __syncthreads();  // every TMEM read is done
+  if (warp == kWarpQK) {
+    if (lane == 0 && !mbar_wait_bounded(&ms.mb_drain, 0, kPollLimit)) record_status(a, 128);
+    __syncwarp();
+    fence_after_sync();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(mla_decode_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e != cudaSuccess) return e;
+  const int head_blocks = (a.num_heads + kNH - 1) / kNH;
+  const dim3 grid = a.balanced ? dim3(a.num_splits, 1, head_blocks) : dim3(a.num_splits, a.batch, head_blocks);
+  mla_decode_fp4_kernel<<<grid, kThreads, kSmem, stream>>>(a, maps);
+  return cudaGetLastError();
+}
+
+}  // namespace kimi

@@ -177,6 +177,32 @@ __device__ __forceinline__ void mma_f8f6f4_ss(uint32_t d_tmem, uint64_t a_desc, 
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// Block-scaled e2m1 x e2m1 MMA (kind::mxf4, one e8m0 scale per 32 K elements,
+// K = 64 per instruction), both operands K-major packed nibbles in shared
+// memory (element 2j in the low nibble of byte j, as in the MXFP4 cache).
+// The scale factors sit in TMEM: for an operand row r (of A's M or B's N),
+// scale block k4 (four consecutive 32-element groups, K = 128) occupies one
+// 32-bit column per 32 rows, column c0 + r / 32 of lane r % 32 holding the
+// four e8m0 bytes of groups 4 k4 .. 4 k4 + 3 of row r, copied identically
+// into all four 32-lane quarters.  `sfa` / `sfb` are the TMEM addresses of
+// that block's first column with the byte of the instruction's first group
+// (0 or 2) in bits 30-31; the same byte index goes into the descriptor.
+__device__ __forceinline__ void mma_mxf4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
+}
+
+// Instruction descriptor of kind::mxf4 (e2m1 operands, e8m0 scales, M = 128,
+// K = 64, fp32 accumulator): scale byte index of A in bits 29-30, of B in 4-5.
+__host__ __device__ constexpr uint32_t instr_desc_mxf4(uint32_t n, uint32_t a_sf_byte, uint32_t b_sf_byte) {
+  return (b_sf_byte << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+         (a_sf_byte << 29);
+}
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05.mma of this
 // thread have completed.
 __device__ __forceinline__ void mma_commit(uint64_t* mbar) {
@@ -195,6 +221,30 @@ __device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
 
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(mbar)), "r"(bytes)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tensor maps encoded on the host; no cluster multicast)
+// ---------------------------------------------------------------------------
+
+// 2-D tiled load of one box at element coordinates (x, y) into shared memory;
+// the box's bytes count towards the mbarrier's transaction count.  Box
+// elements outside the tensor are filled with zeros.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tensor_map, int x, int y, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+          "r"(smem_addr(dst)),
+      "l"(tensor_map), "r"(x), "r"(y), "r"(smem_addr(mbar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const void* tensor_map) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(tensor_map) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, uint32_t parity) {
@@ -272,6 +322,18 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2_f16x2(uint32_t byte) {
       "cvt.rn.f16x2.e2m1x2 %0, b;\n\t}\n"
       : "=r"(out)
       : "r"(byte));
+  return out;
+}
+
+// Two floats -> two e2m1 codes in one byte (round to nearest even,
+// saturating to +-6); `lo` lands in the low nibble.
+__device__ __forceinline__ uint32_t cvt_f32x2_e2m1x2(float lo, float hi) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\t"
+      "cvt.u32.u8 %0, t;\n\t}\n"
+      : "=r"(out)
+      : "f"(lo), "f"(hi));
   return out;
 }
 

@@ -41,6 +41,9 @@ if ROOT not in sys.path:
 METRIC = "MLA decode µs/layer & achieved HBM TB/s (Kimi-K2, b64 ctx8K) at 1/2/4/8 B200"
 HEADS, BATCH, CTX, PAGE = 64, 64, 8192, 64
 SM_SCALE = 1.0 / math.sqrt(192.0)
+# stage-1 kernel the library launches (KIMI_MLA_DECODE_KERNEL selects the comparison kernels)
+STAGE1_KERNEL = {"tc": "mla_decode_tc_kernel", "mma": "mla_decode_mma_kernel"}.get(
+    os.environ.get("KIMI_MLA_DECODE_KERNEL", ""), "mla_decode_fp4_kernel")
 TOKEN_BYTES_ALGO = 256 + 16 + 128  # nibbles + e8m0 scales + bf16 RoPE per token
 FALLBACK_HBM_GBS = 6650.0
 WORKLOAD = (f"Kimi-K2 MXFP4 MLA decode: {HEADS} heads, batch {BATCH} per GPU, ctx {CTX} every sequence, "
@@ -347,7 +350,7 @@ def run_ours(args, rank, world, local_rank):
                         "copied back every step"},
         "gpu_launches": args.steps * 2,
         "kernels": {"stage1_ms": round(stage1_avg, 5), "merge_ms": round(red_ms, 5),
-                    "launches_per_step": ["mla_decode_tc_kernel", "mla_reduce_kernel"]},
+                    "launches_per_step": [STAGE1_KERNEL, "mla_reduce_kernel"]},
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS hbm_gbs)"
                      if peak_kind == "measured" else "fallback",

@@ -154,19 +154,26 @@ __device__ __forceinline__ void record_status(const DecodeArgs& a, int bits) {
   if (a.status) atomicOr(a.status, bits);
 }
 
-// Per-thread bounded wait; on give-up records the failure and raises the abort word.
+// Per-thread bounded wait: one plain probe first (a phase that has already
+// completed costs only that), then polls with a suspend-time hint; on give-up
+// records the failure and raises the abort word.
 __device__ __forceinline__ bool wait_phase(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit) {
+  if (mbar_try_wait(mb, parity)) return true;
   if (mbar_wait_or_abort(mb, parity, kPollLimit, &ms.abort_flag)) return true;
   if (atomicExch(&ms.abort_flag, 1) == 0) record_status(a, bit);
   return false;
 }
 
-// Warp-uniform bounded wait: lane 0 polls, the warp gets its verdict.
+// Warp-uniform bounded wait.  Every lane probes (one warp-wide instruction per
+// poll) and a vote makes the verdict uniform: an elected lane polling inside a
+// divergent branch and broadcasting its verdict costs several hundred cycles
+// per call even when the phase is already complete.
 __device__ __forceinline__ bool warp_wait(uint64_t* mb, uint32_t parity, Misc& ms, const DecodeArgs& a, int bit,
                                           int lane) {
-  bool ok = true;
-  if (lane == 0) ok = wait_phase(mb, parity, ms, a, bit);
-  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (__all_sync(0xffffffffu, mbar_try_wait(mb, parity))) return true;
+  const bool ok = __all_sync(0xffffffffu, mbar_wait_or_abort(mb, parity, kPollLimit, &ms.abort_flag));
+  if (!ok && lane == 0 && atomicExch(&ms.abort_flag, 1) == 0) record_status(a, bit);
+  return ok;
 }
 
 // Page rows (y coordinates of the cache tensor maps) of the two pages of the
@@ -629,11 +636,6 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
 #pragma unroll
         for (int u = 0; u < 4; ++u) t[j + u] = tvalid ? fmaf(t[j + u], c_log2, -rv[u]) : -CUDART_INF_F;
       }
-      // PV(j-1) must be complete before O is rescaled or read, or P'' is overwritten
-      if (ok && tile > 0) {
-        const uint32_t pp = static_cast<uint32_t>((tile - 1) & 1);
-        ok = warp_wait(&ms.mb_pvq[3], pp, ms, a, 2, lane);
-      }
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j) t[j] = -CUDART_INF_F;
@@ -648,6 +650,18 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
         bar_or(kBarSoftmax, kSoftmaxThreads, !ok || first || tmaxv > 8.5f || sigma_cur != sigma_prev);
     if (need && bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) break;
     fence_after_sync();
+    // PV(j-1) must be complete before O is rescaled or P'' is overwritten.  The
+    // wait sits right before the first of those, so the score work of tile j
+    // overlaps PV(j-1).  A wait that gives up has raised the abort word; the
+    // warp keeps to the common barrier sequence and leaves at the next check.
+    bool pv_prev_done = tile == 0;
+    auto wait_pv_prev = [&]() {
+      if (!pv_prev_done) {
+        warp_wait(&ms.mb_pvq[3], static_cast<uint32_t>((tile - 1) & 1), ms, a, 2, lane);
+        fence_after_sync();
+        pv_prev_done = true;
+      }
+    };
     if (need) {
       float v[32];
 #pragma unroll
@@ -670,6 +684,7 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
       if (!first) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) l_part[j] *= ms.beta[32 * hf + j];
+        wait_pv_prev();
 #pragma unroll 1
         for (int cc = 0; cc < 2; ++cc) {
           const int c = 2 * hf + cc;
@@ -710,6 +725,7 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
           pl[j / 4] |= static_cast<uint32_t>(l8) << 16;
         }
       }
+      wait_pv_prev();
       const int prow = (st >> 3) * kPRow + (st & 7) * 16;
       *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf) * 128) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
       *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf + 1) * 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);

@@ -127,7 +127,7 @@ struct Misc {
   uint64_t mb_kpefree;       // RoPE MMAs of the tile in the k_pe buffer complete (commit)
   uint64_t mb_sfull;         // QK(j) complete (commit)
   uint64_t mb_sfree;         // S(j) read out of TMEM (8 softmax warps)
-  uint64_t mb_pfull;         // P''(j) written, O rescaled (8 softmax warps)
+  uint64_t mb_pfull[4];      // P''(j) token quarter k written, O rescaled (2 softmax warps)
   uint64_t mb_qready;        // Q terms, their scales and q_pe of a piece written (8 softmax warps)
   uint64_t mb_drain;         // each issuer's last commit (3 arrivals)
   SchedScratch sched;        // balanced mode: block-scan scratch
@@ -194,9 +194,10 @@ __device__ __forceinline__ void tile_rows(const DecodeArgs& a, const Cursor& c, 
 // TMA producer (warp 19, lane 0)
 // ---------------------------------------------------------------------------
 // Nibbles go to a two-stage ring (tile j waits for QK(j - 2) and the loaders'
-// V'' of tile j - 2), scales to a four-slot ring two tiles ahead of the
+// V'' of tile j - 2), scales to a four-slot ring up to two tiles ahead of the
 // nibbles (the loaders need tile j + 1's scales while converting tile j), k_pe
-// to one buffer (tile j waits for the RoPE MMAs of tile j - 1).
+// to one buffer (tile j waits for the RoPE MMAs of tile j - 1).  Tile 0's
+// scales, nibbles and k_pe are issued before anything else.
 __device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArgs& a, const CacheMaps& maps) {
   prefetch_tensormap(&maps.kv);
   prefetch_tensormap(&maps.sc);
@@ -217,12 +218,15 @@ __device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArg
     ++sc_issued;
     cursor_next(a, sc_cur);
   };
-  // L2 prefetch of the tiles the TMA loads reach later (tiles 0 and 1 are loaded at once)
+  // L2 prefetch of the tiles the TMA loads reach later (tiles 0 and 1 are loaded at once).
+  // Each call reads the page ids of at most two more tiles: those reads stall
+  // this thread, and the nibble loads of the next tile must not wait on them.
   pc = cur;
   cursor_next(a, pc);
   cursor_next(a, pc);
   int prefetched = 2;
   auto prefetch_upto = [&](int upto) {
+    upto = min(upto, prefetched + 2);
     while (prefetched < min(upto, sc.count)) {
       int y[2];
       tile_rows(a, pc, y);
@@ -237,8 +241,9 @@ __device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArg
       cursor_next(a, pc);
     }
   };
-  for (int t = 0; t < min(2, sc.count); ++t) load_scales();
-  prefetch_upto(2 + kPrefetchTiles);
+  // Only tile 0's scales go first: its nibbles follow at once (the page ids
+  // are then cached), the next scales after them.
+  load_scales();
   int issued = 0;
   for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
     const int s = j & 1;
@@ -247,7 +252,6 @@ __device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArg
       const uint32_t par = static_cast<uint32_t>(((j - 2) >> 1) & 1);
       if (!wait_phase(&ms.mb_qkdone[s], par, ms, a, 256) || !wait_phase(&ms.mb_nibread[s], par, ms, a, 256)) break;
     }
-    if (j + 2 < sc.count) load_scales();
     int y[2];
     tile_rows(a, cur, y);
     const int slots = (y[0] != -1 ? 1 : 0) + (y[1] != -1 ? 1 : 0);
@@ -259,13 +263,21 @@ __device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArg
       tma_load_2d(nib, &maps.kv, 0, y[slot], &ms.mb_rawfull[s]);
       tma_load_2d(nib + kNibBlock, &maps.kv, 128, y[slot], &ms.mb_rawfull[s]);
     }
-    // k_pe (one buffer): free once the RoPE MMAs of tile j - 1 are complete
-    if (j >= 1 && !wait_phase(&ms.mb_kpefree, static_cast<uint32_t>((j - 1) & 1), ms, a, 256)) break;
-    mbar_arrive_expect_tx(&ms.mb_kpefull, static_cast<uint32_t>(slots * 64 * 128));
+    auto load_kpe = [&]() {
+      mbar_arrive_expect_tx(&ms.mb_kpefull, static_cast<uint32_t>(slots * 64 * 128));
 #pragma unroll
-    for (int slot = 0; slot < 2; ++slot) {
-      if (y[slot] == -1) continue;
-      tma_load_2d(sm + kOffKpe + slot * (64 * 128), &maps.kv, kNibbleBytes, y[slot], &ms.mb_kpefull);
+      for (int slot = 0; slot < 2; ++slot) {
+        if (y[slot] == -1) continue;
+        tma_load_2d(sm + kOffKpe + slot * (64 * 128), &maps.kv, kNibbleBytes, y[slot], &ms.mb_kpefull);
+      }
+    };
+    if (j == 0) load_kpe();
+    // scales run up to two tiles ahead of the nibbles
+    while (sc_issued < min(j + 3, sc.count)) load_scales();
+    // k_pe (one buffer): free once the RoPE MMAs of tile j - 1 are complete
+    if (j >= 1) {
+      if (!wait_phase(&ms.mb_kpefree, static_cast<uint32_t>((j - 1) & 1), ms, a, 256)) break;
+      load_kpe();
     }
     issued = j + 1;
     prefetch_upto(j + 3 + kPrefetchTiles);
@@ -350,12 +362,11 @@ __device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
   cursor_start(a, sc, cur);
   for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
     const uint32_t par = static_cast<uint32_t>(j & 1);
-    if (!warp_wait(&ms.mb_pfull, par, ms, a, 32, lane)) break;
     const bool fresh = cursor_first(cur);  // the piece's first PV starts the accumulator
     bool ok = true;
 #pragma unroll 1
     for (int k = 0; k < 4 && ok; ++k) {
-      ok = warp_wait(&ms.mb_vfull[k], par, ms, a, 32, lane);
+      ok = warp_wait(&ms.mb_pfull[k], par, ms, a, 32, lane) && warp_wait(&ms.mb_vfull[k], par, ms, a, 32, lane);
       if (!ok) break;
       fence_after_sync();
       if (lane == 0) {
@@ -654,12 +665,19 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     // wait sits right before the first of those, so the score work of tile j
     // overlaps PV(j-1).  A wait that gives up has raised the abort word; the
     // warp keeps to the common barrier sequence and leaves at the next check.
-    bool pv_prev_done = tile == 0;
-    auto wait_pv_prev = [&]() {
+    bool pv_prev_done = tile == 0, pvq_prev_done = tile == 0;
+    auto wait_pv_prev = [&]() {  // all of PV(j-1)
       if (!pv_prev_done) {
         warp_wait(&ms.mb_pvq[3], static_cast<uint32_t>((tile - 1) & 1), ms, a, 2, lane);
         fence_after_sync();
-        pv_prev_done = true;
+        pv_prev_done = pvq_prev_done = true;
+      }
+    };
+    auto wait_pvq_prev = [&]() {  // PV(j-1) of this warp's token quarter (its P'' rows)
+      if (!pvq_prev_done) {
+        warp_wait(&ms.mb_pvq[q], static_cast<uint32_t>((tile - 1) & 1), ms, a, 2, lane);
+        fence_after_sync();
+        pvq_prev_done = true;
       }
     };
     if (need) {
@@ -725,7 +743,7 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
           pl[j / 4] |= static_cast<uint32_t>(l8) << 16;
         }
       }
-      wait_pv_prev();
+      wait_pvq_prev();
       const int prow = (st >> 3) * kPRow + (st & 7) * 16;
       *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf) * 128) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
       *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf + 1) * 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
@@ -735,7 +753,7 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     fence_proxy_async_smem();
     fence_before_sync();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&ms.mb_pfull);
+    if (lane == 0) mbar_arrive(&ms.mb_pfull[q]);
 
     if (!cursor_last(cur)) continue;
     // ---------------- epilogue of the piece ----------------
@@ -767,28 +785,46 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
       a.seq_meta[cur.b] = make_int2(blockIdx.x, last_cta);
     }
     named_bar(kBarSoftmax, kSoftmaxThreads);
-    // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane
+    // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane.
+    // Each 32-latent x 32-head unit is transposed through this warp's 2 KB of
+    // the P'' area (idle: the piece's last PV is complete) into rows of
+    // 8 latents per head, stored as 16-byte vectors.
+    const bool vec = !direct || ((reinterpret_cast<uintptr_t>(a.o) |
+                                  static_cast<uintptr_t>(a.o_stride_b * 2) |
+                                  static_cast<uintptr_t>(a.o_stride_h * 2)) & 15) == 0;
+    uint8_t* stage = sm + kOffP + warp * 2048;
 #pragma unroll 1
     for (int cc = 0; cc < 2; ++cc) {
       const int c = 2 * hf + cc;
-      const int d = 128 * c + 32 * q + lane;
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t vv[32];
         tmem_ld32(tmem + lane_base + kColO + 64 * c + 32 * hh, vv);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int hd = 32 * hh + j;
+        for (int j = 0; j < 32; ++j)
+          reinterpret_cast<__nv_bfloat16*>(stage)[32 * j + lane] =
+              __float2bfloat16_rn(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int idx = 32 * i + lane, hd = 32 * hh + (idx >> 2), d0 = 128 * c + 32 * q + 8 * (idx & 3);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + 16 * idx);
           if (hd < heads_here) {
-            const float val = __uint_as_float(vv[j]) * ms.alpha[hd];
             const int hq = head_base + hd;
-            if (direct)
-              a.o[cur.b * a.o_stride_b + hq * a.o_stride_h + d] = __float2bfloat16_rn(val);
-            else
-              a.partial_o[(slot * a.num_heads + hq) * kLatent + d] = __float2bfloat16_rn(val);
+            __nv_bfloat16* dst = direct ? a.o + cur.b * a.o_stride_b + hq * a.o_stride_h + d0
+                                        : a.partial_o + (slot * a.num_heads + hq) * kLatent + d0;
+            if (vec) {
+              *reinterpret_cast<uint4*>(dst) = v;
+            } else {
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                dst[e] = __ushort_as_bfloat16(static_cast<unsigned short>(w[e >> 1] >> (16 * (e & 1))));
+            }
           }
         }
+        __syncwarp();  // the stage is rewritten by the next unit
       }
     }
     // O and alpha are read before the next piece's PV / rescale touch them
@@ -862,7 +898,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
     mbar_init(&ms.mb_kpefree, 1);
     mbar_init(&ms.mb_sfull, 1);
     mbar_init(&ms.mb_sfree, kSoftmaxWarps);
-    mbar_init(&ms.mb_pfull, kSoftmaxWarps);
+    for (int i = 0; i < 4; ++i) mbar_init(&ms.mb_pfull[i], 2);
     mbar_init(&ms.mb_qready, kSoftmaxWarps);
     mbar_init(&ms.mb_drain, 3);
     ms.abort_flag = 0;

@@ -151,11 +151,13 @@ inline size_t round256(size_t n) { return (n + 255) & ~static_cast<size_t>(255);
 
 // Workspace: partial outputs [slots, heads, 512] bf16 (each normalised by its own
 // softmax sum, so bf16 costs one rounding like the output's), log-sum-exps [slots,
-// heads] fp32, then (balanced mode) [batch] int2 CTA spans.  Split mode has
-// batch * S slots (none for S = 1), balanced mode batch + ctas.
+// heads] fp32, then (balanced mode) [batch] int2 CTA spans, then (fp4 kernel)
+// the Q operand images [batch][head blocks] of kQImageBytes.  Split mode has
+// batch * S slots (none for S = 1, and no workspace at all: the fp4 kernel
+// then quantises Q itself), balanced mode batch + ctas.
 struct Layout {
-  size_t slots, po_bytes, lse_bytes, meta_bytes;
-  size_t total() const { return po_bytes + lse_bytes + meta_bytes; }
+  size_t slots, po_bytes, lse_bytes, meta_bytes, qimg_bytes;
+  size_t total() const { return po_bytes + lse_bytes + meta_bytes + qimg_bytes; }
 };
 
 Layout workspace_layout(int64_t batch, int64_t heads, const Plan& plan) {
@@ -165,6 +167,8 @@ Layout workspace_layout(int64_t batch, int64_t heads, const Plan& plan) {
   l.po_bytes = round256(l.slots * heads * kLatent * sizeof(__nv_bfloat16));
   l.lse_bytes = round256(l.slots * heads * sizeof(float));
   l.meta_bytes = plan.balanced ? round256(static_cast<size_t>(batch) * 2 * sizeof(int32_t)) : 0;
+  if (stage1_kernel() == Stage1::kFp4)
+    l.qimg_bytes = round256(static_cast<size_t>(batch) * ((heads + 63) / 64) * kimi::kQImageBytes);
   return l;
 }
 
@@ -250,6 +254,7 @@ int prepare(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_byte
   a.partial_o = need ? reinterpret_cast<__nv_bfloat16*>(ws) : nullptr;
   a.partial_lse = need ? reinterpret_cast<float*>(ws + lay.po_bytes) : nullptr;
   a.seq_meta = plan.balanced ? reinterpret_cast<int2*>(ws + lay.po_bytes + lay.lse_bytes) : nullptr;
+  a.q_img = lay.qimg_bytes ? ws + lay.po_bytes + lay.lse_bytes + lay.meta_bytes : nullptr;
   a.batch = p->batch;
   a.num_heads = p->num_heads;
   a.num_splits = plan.ctas;
@@ -267,7 +272,13 @@ int launch_stage1(const Prepared& pr, cudaStream_t s) {
   switch (stage1_kernel()) {
     case Stage1::kMma: return cuda_status(kimi::launch_decode_mma(pr.args, s));
     case Stage1::kTc: return cuda_status(kimi::launch_decode_tc(pr.args, s));
-    default: return cuda_status(kimi::launch_decode_fp4(pr.args, pr.maps, s));
+    default: {
+      if (pr.args.q_img) {
+        const int st = cuda_status(kimi::launch_q_prep_fp4(pr.args, s));
+        if (st != KIMI_OK) return st;
+      }
+      return cuda_status(kimi::launch_decode_fp4(pr.args, pr.maps, s));
+    }
   }
 }
 

@@ -18,6 +18,14 @@ constexpr int kTokenBytes = 384;  // nibbles + RoPE per token in kv_buffer
 constexpr int kScaleBytes = 16;
 constexpr int kPageBytes = kPageSize * kTokenBytes;        // 24576
 constexpr int kPageScaleBytes = kPageSize * kScaleBytes;   // 1024
+// Q operands of the fp4 kernel for one (sequence, 64-head block), as the
+// shared-memory images its QK^T MMAs read: three block-scaled e2m1 terms
+// (2 K blocks x 192 rows x 128 B, 128-byte swizzle), q_pe (64 rows x 128 B,
+// same swizzle), then the terms' e8m0 scales as [192 rows][16 blocks].
+constexpr int kQTermBytes = 2 * 192 * 128;   // 49152
+constexpr int kQPeBytes = 64 * 128;          // 8192
+constexpr int kQScaleBytes = 192 * 16;       // 3072
+constexpr int kQImageBytes = kQTermBytes + kQPeBytes + kQScaleBytes;  // 60416
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -73,6 +81,7 @@ struct DecodeArgs {
   float* partial_lse;  // [batch, splits, heads]
   int* status;         // optional device word: bits set when a bounded wait gave up
   int2* seq_meta;      // balanced mode: [batch] (first CTA, last CTA) of each sequence's tiles
+  const uint8_t* q_img;  // fp4 kernel: [batch][head blocks] Q operand images (kQImageBytes each), or null
   int batch;
   int num_heads;
   int num_splits;      // split mode: splits per sequence
@@ -107,6 +116,8 @@ cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream);
+// Writes a.q_img (one CTA per sequence and head block); the fp4 kernel launched after it reads the images.
+cudaError_t launch_q_prep_fp4(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_reduce(const ReduceArgs& a, cudaStream_t stream);
 
 }  // namespace kimi

@@ -129,6 +129,7 @@ struct Misc {
   uint64_t mb_sfree;         // S(j) read out of TMEM (8 softmax warps)
   uint64_t mb_pfull[4];      // P''(j) token quarter k written, O rescaled (2 softmax warps)
   uint64_t mb_qready;        // Q terms, their scales and q_pe of a piece written (8 softmax warps)
+  uint64_t mb_qload;         // Q image of a piece landed (bulk copy; Q images in the workspace only)
   uint64_t mb_drain;         // each issuer's last commit (3 arrivals)
   SchedScratch sched;        // balanced mode: block-scan scratch
   uint32_t tmem_base;
@@ -144,6 +145,8 @@ constexpr int kSmem = kOffMisc + static_cast<int>(sizeof(Misc));
 static_assert(kSmem <= 232448, "shared memory budget");
 static_assert(kOffMisc % 16 == 0 && offsetof(Misc, R) % 16 == 0, "per-head arrays are read with 16-byte loads");
 static_assert(kOffP + 192 * kScaleBytes <= kOffMisc, "Q scale staging fits in P''");
+static_assert(kQTermBytes == 2 * kQBlock && kOffQpe == kOffQ + kQTermBytes && kQPeBytes == 64 * 128,
+              "the Q image's terms and q_pe land with one bulk copy");
 
 __device__ __forceinline__ uint8_t* smem_base() {
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
@@ -312,6 +315,7 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
     if (j > 0 && !warp_wait(&ms.mb_sfree, static_cast<uint32_t>((j - 1) & 1), ms, a, 16, lane)) break;
     if (cursor_first(cur)) {
       if (!warp_wait(&ms.mb_qready, static_cast<uint32_t>(pieces & 1), ms, a, 16, lane)) break;
+      if (a.q_img && !warp_wait(&ms.mb_qload, static_cast<uint32_t>(pieces & 1), ms, a, 16, lane)) break;
       ++pieces;
     }
     fence_after_sync();
@@ -504,83 +508,111 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, in
 }
 
 // ---------------------------------------------------------------------------
-// Q of one sequence (softmax threads 0..255: 4 per head; part p handles the
-// 32-element blocks 4p .. 4p + 3 of the latent and 16-byte chunks 2p, 2p + 1 of q_pe)
+// Q of one sequence (256 threads: 4 per head; part p handles the 32-element
+// blocks 4p .. 4p + 3 of the latent and 16-byte chunks 2p, 2p + 1 of q_pe).
+// Writes the QK operand images: the terms at qdst (the layout of kOffQ), q_pe
+// at pedst (the layout of kOffQpe) and the terms' scale bytes at sfdst as
+// [192 rows][16 blocks].  Used in shared memory by the decode kernel (no
+// workspace) and in global memory by the Q prep kernel.
 // ---------------------------------------------------------------------------
-__device__ void build_q(uint8_t* sm, Misc& ms, uint32_t tmem, const DecodeArgs& a, int b, int head_base,
-                        int heads_here, int warp, int lane) {
-  const int tid = threadIdx.x;
+__device__ __forceinline__ void q_block(const uint4 (&v)[4], int h, int bl, uint8_t* qdst, uint8_t* sfdst) {
+  float x[32];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t ws[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[8 * k + 2 * i] = __uint_as_float(ws[i] << 16);
+      x[8 * k + 2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    // smallest e with amax <= 6 * 2^e: amax = 1.m * 2^f -> f - 2, or f - 1 when 1.m > 1.5
+    const uint32_t ab = __float_as_uint(amax);
+    int e = static_cast<int>(ab >> 23) - 129 + ((ab & 0x7FFFFFu) > 0x400000u ? 1 : 0);
+    e = max(-127, min(126, e));
+    const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+    const float scl = e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : __uint_as_float(0x00400000u);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t byte = cvt_f32x2_e2m1x2(x[2 * i] * inv, x[2 * i + 1] * inv);
+      w[i >> 2] |= byte << (8 * (i & 3));
+      if (t < 2) {
+        const uint32_t h2 = cvt_e2m1x2_f16x2(byte);
+        x[2 * i] -= __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu))) * scl;
+        x[2 * i + 1] -= __half2float(__ushort_as_half(static_cast<unsigned short>(h2 >> 16))) * scl;
+      }
+    }
+    const int n = 64 * t + h;
+    *reinterpret_cast<uint4*>(qdst + (bl >> 3) * kQBlock + (n >> 3) * 1024 + sw128_offset(n & 7, bl & 7)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+    sfdst[n * kScaleBytes + bl] = static_cast<uint8_t>(e + 127);
+  }
+}
+
+__device__ void q_operands(const DecodeArgs& a, int b, int head_base, int heads_here, int tid, uint8_t* qdst,
+                           uint8_t* pedst, uint8_t* sfdst) {
   const int h = tid >> 2, part = tid & 3;
   const bool live = h < heads_here;
   const __nv_bfloat16* qrow = a.q + b * a.q_stride_b + (head_base + h) * a.q_stride_h;
-  uint8_t* sf_stage = sm + kOffP;  // [192 rows][16] e8m0 (P'' is free at a piece start)
 #pragma unroll 1
   for (int blk = 0; blk < 4; ++blk) {
-    const int bl = 4 * part + blk;
-    float x[32];
-    {
-      uint4 v[4];
+    uint4 v[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        v[k] = live ? *reinterpret_cast<const uint4*>(qrow + 32 * bl + 8 * k) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t ws[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          x[8 * k + 2 * i] = __uint_as_float(ws[i] << 16);
-          x[8 * k + 2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < 3; ++t) {
-      float amax = 0.f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
-      // smallest e with amax <= 6 * 2^e: amax = 1.m * 2^f -> f - 2, or f - 1 when 1.m > 1.5
-      const uint32_t ab = __float_as_uint(amax);
-      int e = static_cast<int>(ab >> 23) - 129 + ((ab & 0x7FFFFFu) > 0x400000u ? 1 : 0);
-      e = max(-127, min(126, e));
-      const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
-      const float scl = e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : __uint_as_float(0x00400000u);
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t byte = cvt_f32x2_e2m1x2(x[2 * i] * inv, x[2 * i + 1] * inv);
-        w[i >> 2] |= byte << (8 * (i & 3));
-        if (t < 2) {
-          const uint32_t h2 = cvt_e2m1x2_f16x2(byte);
-          x[2 * i] -= __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu))) * scl;
-          x[2 * i + 1] -= __half2float(__ushort_as_half(static_cast<unsigned short>(h2 >> 16))) * scl;
-        }
-      }
-      const int n = 64 * t + h;
-      *reinterpret_cast<uint4*>(sm + kOffQ + (bl >> 3) * kQBlock + (n >> 3) * 1024 + sw128_offset(n & 7, bl & 7)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
-      sf_stage[n * kScaleBytes + bl] = static_cast<uint8_t>(e + 127);
-    }
+    for (int k = 0; k < 4; ++k) v[k] = ldg_stream_if(qrow + 32 * (4 * part + blk) + 8 * k, live);
+    q_block(v, h, 4 * part + blk, qdst, sfdst);
   }
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int c = 2 * part + k;
-    const uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + kLatent + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(sm + kOffQpe + (h >> 3) * 1024 + sw128_offset(h & 7, c)) = v;
+  for (int k = 0; k < 2; ++k)
+    *reinterpret_cast<uint4*>(pedst + (h >> 3) * 1024 + sw128_offset(h & 7, 2 * part + k)) =
+        ldg_stream_if(qrow + kLatent + 8 * (2 * part + k), live);
+}
+
+// B scale factors of the Q terms into TMEM (softmax warps 0-3, one TMEM lane
+// quarter each): column 8 k4 + n1 of lane n0 (every quarter alike) holds the
+// scale word k4 of row n0 + 32 n1 (rows >= 192 are not read).  `global` says
+// whether sf ([192][16] bytes) lies in global memory.
+__device__ __forceinline__ void store_q_scales(uint32_t tmem, const uint8_t* sf, bool global, int warp, int lane) {
+  uint32_t u[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int n = lane + 32 * (i & 7);
+    const uint8_t* src = sf + min(n, 191) * kScaleBytes + 4 * (i >> 3);
+    const uint32_t w = global ? static_cast<uint32_t>(ldg_s32_or(reinterpret_cast<const int32_t*>(src), true, 0))
+                              : *reinterpret_cast<const uint32_t*>(src);
+    u[i] = n < 192 ? w : 0x7F7F7F7Fu;
   }
-  if (part == 0) ms.R[h] = 0.f;
+  tmem_st32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + kColSfb, u);
+  tmem_st_wait();
+}
+
+// Q operands of a new piece's sequence (softmax threads).  With Q images in
+// the workspace: one bulk copy of the terms and q_pe (completing mb_qload)
+// and the scale factors from global memory; otherwise quantised here.
+__device__ void build_q(uint8_t* sm, Misc& ms, uint32_t tmem, const DecodeArgs& a, int b, int head_base,
+                        int heads_here, int warp, int lane) {
+  const int tid = threadIdx.x;
+  if (a.q_img) {
+    const uint8_t* img = a.q_img + (static_cast<int64_t>(b) * gridDim.z + blockIdx.z) * kQImageBytes;
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the Q prep grid is complete (no-op later)
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&ms.mb_qload, kQTermBytes + kQPeBytes);
+      bulk_load(sm + kOffQ, img, kQTermBytes + kQPeBytes, &ms.mb_qload);
+    }
+    if (tid < kNH) ms.R[tid] = 0.f;
+    if (warp < 4) store_q_scales(tmem, img + kQTermBytes + kQPeBytes, true, warp, lane);
+    return;
+  }
+  uint8_t* sf_stage = sm + kOffP;  // [192 rows][16] e8m0 (P'' is free at a piece start)
+  q_operands(a, b, head_base, heads_here, tid, sm + kOffQ, sm + kOffQpe, sf_stage);
+  if ((tid & 3) == 0) ms.R[tid >> 2] = 0.f;
   named_bar(kBarSoftmax, kSoftmaxThreads);  // the scale bytes are staged
-  if (warp < 4) {
-    // B scale factors: column 8 k4 + n1 of lane n0 (every quarter alike) holds
-    // the scale word k4 of row n0 + 32 n1 (rows >= 192 are not read)
-    uint32_t u[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int n = lane + 32 * (i & 7);
-      u[i] = n < 192 ? *reinterpret_cast<const uint32_t*>(sf_stage + n * kScaleBytes + 4 * (i >> 3)) : 0x7F7F7F7Fu;
-    }
-    tmem_st32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + kColSfb, u);
-    tmem_st_wait();
-  }
+  if (warp < 4) store_q_scales(tmem, sf_stage, false, warp, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -900,6 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
     mbar_init(&ms.mb_sfree, kSoftmaxWarps);
     for (int i = 0; i < 4; ++i) mbar_init(&ms.mb_pfull[i], 2);
     mbar_init(&ms.mb_qready, kSoftmaxWarps);
+    mbar_init(&ms.mb_qload, 1);
     mbar_init(&ms.mb_drain, 3);
     ms.abort_flag = 0;
     fence_mbar_init();
@@ -942,15 +975,56 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
   }
 }
 
+// Q operand images of every (sequence, head block): one CTA of 1024 threads
+// each, thread (h, bl) quantising the 32-element block bl of head h (and the
+// 16-byte chunk bl < 8 of its q_pe).  It lets the decode kernel launched
+// after it start at once; that kernel waits for this grid before reading
+// the images.
+__global__ void __launch_bounds__(1024) q_prep_fp4_kernel(const __grid_constant__ DecodeArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  const int b = blockIdx.y, head_base = blockIdx.x * kNH;
+  const int h = threadIdx.x >> 4, bl = threadIdx.x & 15;
+  const bool live = h < a.num_heads - head_base;
+  uint8_t* img = const_cast<uint8_t*>(a.q_img) + (static_cast<int64_t>(b) * gridDim.x + blockIdx.x) * kQImageBytes;
+  const __nv_bfloat16* qrow = a.q + b * a.q_stride_b + (head_base + h) * a.q_stride_h;
+  uint4 v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = ldg_stream_if(qrow + 32 * bl + 8 * k, live);
+  const uint4 pe = ldg_stream_if(qrow + kLatent + 8 * (bl & 7), live && bl < 8);
+  q_block(v, h, bl, img, img + kQTermBytes + kQPeBytes);
+  if (bl < 8) *reinterpret_cast<uint4*>(img + kQTermBytes + (h >> 3) * 1024 + sw128_offset(h & 7, bl)) = pe;
+}
+
 }  // namespace
+
+cudaError_t launch_q_prep_fp4(const DecodeArgs& a, cudaStream_t stream) {
+  const dim3 grid((a.num_heads + kNH - 1) / kNH, a.batch);
+  q_prep_fp4_kernel<<<grid, 1024, 0, stream>>>(a);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(mla_decode_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
   const int head_blocks = (a.num_heads + kNH - 1) / kNH;
   const dim3 grid = a.balanced ? dim3(a.num_splits, 1, head_blocks) : dim3(a.num_splits, a.batch, head_blocks);
-  mla_decode_fp4_kernel<<<grid, kThreads, kSmem, stream>>>(a, maps);
-  return cudaGetLastError();
+  if (!a.q_img) {
+    mla_decode_fp4_kernel<<<grid, kThreads, kSmem, stream>>>(a, maps);
+    return cudaGetLastError();
+  }
+  // after the Q prep kernel: start while it runs (everything before the Q
+  // images, the first cache loads included, overlaps it)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mla_decode_fp4_kernel, a, maps);
 }
 
 }  // namespace kimi

@@ -243,6 +243,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tensor_map, i
       : "memory");
 }
 
+// Untiled bulk copy global -> shared of `bytes` (a multiple of 16; both
+// addresses 16-byte aligned); the bytes count towards the mbarrier's
+// transaction count.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(mbar))
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const void* tensor_map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(tensor_map) : "memory");
 }

@@ -35,12 +35,19 @@ def test_status_strings_and_version():
     assert _lib.status_text(-12345) == "unknown status"
 
 
+# Q operand images of the fp4 kernel per (sequence, 64-head block): three e2m1
+# terms (2 x 192 x 128 B), q_pe (64 x 128 B) and the terms' scales (192 x 16 B)
+Q_IMAGE_BYTES = 2 * 192 * 128 + 64 * 128 + 192 * 16
+
+
 def test_workspace_size_arithmetic():
     lib = _lib.load()
-    # explicit splits: partial O (B*S*H*512 bf16) + LSE (B*S*H f32), each rounded to 256 B
+    # explicit splits: partial O (B*S*H*512 bf16) + LSE (B*S*H f32) + the fp4
+    # kernel's Q operand images (B * head blocks * 60416 B), each rounded to 256 B
     b, h, s = 64, 64, 4
     rows = b * s * h
-    expect = ((rows * 512 * 2 + 255) // 256) * 256 + ((rows * 4 + 255) // 256) * 256
+    r256 = lambda n: ((n + 255) // 256) * 256
+    expect = r256(rows * 512 * 2) + r256(rows * 4) + r256(b * 1 * Q_IMAGE_BYTES)
     assert lib.kimi_mla_decode_workspace_size(b, h, s) == expect
     assert lib.kimi_mla_decode_workspace_size(b, h, 1) == 0  # single split writes o directly
     assert lib.kimi_mla_decode_workspace_size(b, 0, 4) == 0  # invalid
@@ -57,7 +64,7 @@ def test_balanced_workspace_size_arithmetic():
         assert g >= 1
         slots = b + g
         r256 = lambda n: ((n + 255) // 256) * 256
-        expect = r256(slots * h * 512 * 2) + r256(slots * h * 4) + r256(b * 8)
+        expect = r256(slots * h * 512 * 2) + r256(slots * h * 4) + r256(b * 8) + r256(b * -(-h // 64) * Q_IMAGE_BYTES)
         assert lib.kimi_mla_decode_workspace_size(b, h, 0) == expect
     assert lib.kimi_mla_decode_num_splits(8, 128, 0) * 2 <= lib.kimi_mla_decode_num_splits(8, 64, 0) + 1
 

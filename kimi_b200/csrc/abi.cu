@@ -282,7 +282,9 @@ int launch_stage1(const Prepared& pr, cudaStream_t s) {
   }
 }
 
-int launch_merge(const Prepared& pr, cudaStream_t s) {
+// `after_stage1`: launched right after this call's stage-1 kernel on the same
+// stream; the fp4 kernel lets it start as its programmatic dependent.
+int launch_merge(const Prepared& pr, cudaStream_t s, bool after_stage1) {
   if (!pr.plan.balanced && pr.plan.ctas == 1) return KIMI_OK;  // stage 1 wrote the output
   const kimi::DecodeArgs& a = pr.args;
   kimi::ReduceArgs r;
@@ -297,6 +299,7 @@ int launch_merge(const Prepared& pr, cudaStream_t s) {
   r.num_splits = pr.plan.ctas;
   r.seq_meta = a.seq_meta;
   r.kv_indptr = a.kv_indptr;
+  r.programmatic = after_stage1 && stage1_kernel() == Stage1::kFp4 ? 1 : 0;
   return cuda_status(kimi::launch_reduce(r, s));
 }
 
@@ -310,7 +313,7 @@ int kimi_mla_decode(const KimiMlaDecodeParams* p, void* workspace, size_t worksp
   if (st != KIMI_OK || p->batch == 0) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = launch_stage1(pr, s);
-  return st != KIMI_OK ? st : launch_merge(pr, s);
+  return st != KIMI_OK ? st : launch_merge(pr, s, true);
 }
 
 int kimi_mla_decode_partial(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, void* stream) {
@@ -324,7 +327,7 @@ int kimi_mla_decode_merge(const KimiMlaDecodeParams* p, void* workspace, size_t 
   Prepared pr;
   const int st = prepare(p, workspace, workspace_bytes, pr);
   if (st != KIMI_OK || p->batch == 0) return st;
-  return launch_merge(pr, static_cast<cudaStream_t>(stream));
+  return launch_merge(pr, static_cast<cudaStream_t>(stream), false);
 }
 
 int kimi_mla_reduce(const KimiMlaReduceParams* p, void* stream) {
@@ -348,6 +351,7 @@ int kimi_mla_reduce(const KimiMlaReduceParams* p, void* stream) {
   r.num_splits = p->num_splits;
   r.seq_meta = nullptr;
   r.kv_indptr = nullptr;
+  r.programmatic = 0;
   return cuda_status(kimi::launch_reduce(r, static_cast<cudaStream_t>(stream)));
 }
 

@@ -109,6 +109,7 @@ struct ReduceArgs {
   int num_splits;             // split mode: slots b * num_splits + s
   const int2* seq_meta;       // balanced mode (non-null): slots b + c, c in [meta.x, meta.y]
   const int32_t* kv_indptr;   // balanced mode: sequences without pages get zeros
+  int programmatic;           // launched as a programmatic dependent of the decode kernel (waits for it)
 };
 
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);

@@ -867,6 +867,10 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
 
 __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __grid_constant__ DecodeArgs a,
                                                                   const __grid_constant__ CacheMaps maps) {
+  // the merge kernel (launched next as a programmatic dependent) may be
+  // scheduled once every CTA of this grid runs; it waits for this grid to
+  // complete before reading anything
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   uint8_t* sm = smem_base();
   Misc& ms = *reinterpret_cast<Misc*>(sm + kOffMisc);
   const int tid = threadIdx.x;

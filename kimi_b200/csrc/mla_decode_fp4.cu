@@ -444,10 +444,15 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, in
       const bool free_ok =
           tt < 2 || warp_wait(&ms.mb_qkdone[s], static_cast<uint32_t>(((tt - 2) >> 1) & 1), ms, a, 64, lane);
       if (free_ok) {
-        uint32_t v[16];
+        uint32_t v[16];  // word k4 of token lane + 32 r1 in v[4 k4 + r1]
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          v[i] = *reinterpret_cast<const uint32_t*>(scb + (lane + 32 * (i & 3)) * kScaleBytes + 4 * (i >> 2));
+        for (int r1 = 0; r1 < 4; ++r1) {
+          const uint4 w = *reinterpret_cast<const uint4*>(scb + (lane + 32 * r1) * kScaleBytes);
+          v[r1] = w.x;
+          v[4 + r1] = w.y;
+          v[8 + r1] = w.z;
+          v[12 + r1] = w.w;
+        }
         tmem_st16(tmem + lane_base + kColSfa + 16 * s, v);
         tmem_st_wait();
       }
@@ -473,15 +478,19 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, in
     const uint8_t* scb = sm + kOffSc + (j % kScSlots) * kScStage;
     const bool raw_ok = warp_wait(&ms.mb_rawfull[s], static_cast<uint32_t>((j >> 1) & 1), ms, a, 64, lane);
     const int nvalid = cursor_valid(cur);
-    // V'' quarter k: warp lw converts tokens 32k + 4 lw .. + 3, lane l the
-    // 32-element group 8h + (l % 8) of token 32k + 4 lw + l / 8, h = 0, 1
+    // V'' quarter k: warp lw converts 4 tokens of the quarter's 8-token atom
+    // lw / 2, rows {0, 2, 5, 7} (lw even) or {1, 3, 4, 6} (lw odd); lane l
+    // the 32-element groups 8h + c, h = 0, 1, with c % 4 = l % 4 (bits 0-1),
+    // c / 4 = bit 4, and the row chosen by bits 2-3.  Every 8-lane phase of a
+    // 16-byte access then meets 8 distinct bank groups, for the swizzled
+    // nibble loads (c ^ row) and the V'' stores (2 (c % 4) ^ row) alike.
 #pragma unroll 1
     for (int k = 0; k < 4; ++k) {
       const bool slot_ok =
           raw_ok && (j == 0 || warp_wait(&ms.mb_pvq[k], static_cast<uint32_t>((j - 1) & 1), ms, a, 64, lane));
       if (slot_ok) {
-        const int c = lane & 7;
-        const int t = 32 * k + 4 * lw + (lane >> 3);
+        const int c = (lane & 3) | ((lane >> 2) & 4);
+        const int t = 32 * k + 8 * (lw >> 1) + (((2 * ((lane >> 3) & 1)) | (lw & 1)) ^ (5 * ((lane >> 2) & 1)));
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const uint4 nb =

@@ -330,7 +330,7 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
       // and starts the columns of terms 1 and 2
       const uint32_t sA = smem_addr(sm + kOffNib + s * kNibStage);
       const uint32_t sfa0 = tmem + kColSfa + 16 * s, sfb0 = tmem + kColSfb;
-#pragma unroll 1
+#pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t koff = (k & 3) * 32;
         const uint32_t byte = 2 * (k & 1);

@@ -199,6 +199,47 @@ typedef struct KimiKvAppendParams {
 
 KIMI_API int kimi_mxfp4_kv_append(const KimiKvAppendParams* params, void* stream);
 
+/* The decode step before attention, fused into one launch.  Replaces the
+ * reference's k_up_proj BMM + RoPE + cache write (`MLAAttention.fused_kv_bmm`
+ * and `fused_qk_rope_concat_and_cache_mla`, patches/atom-optimizations.patch:468-639):
+ *   q_out[t, h, :512] = q_nope[t, h, :] @ w_uk[h]          (q absorbed into the latent)
+ *   q_out[t, h, 512:] = rope(q_pe[t, h, :], positions[t])
+ *   cache[slot_mapping[t]] = MXFP4(kv_c[t]) ++ rope(k_pe[t], positions[t])
+ * RoPE: 32 frequency pairs (x[i], x[i+32]) when is_neox, else (x[2i], x[2i+1]);
+ * (a, b) -> (a cos - b sin, b cos + a sin) with cos / sin float32
+ * [max_position, 32] indexed by the position.  A token whose slot is negative
+ * or out of range, or whose position is out of range, is not written to the
+ * cache; an out-of-range position also zeroes its q_out RoPE part.  Element
+ * strides: q_nope / q_pe / q_out per token and per head, kv_c / k_pe per
+ * token, all multiples of 8; w_uk is contiguous [num_heads, 128, 512]. */
+typedef struct KimiQAbsorbParams {
+  const void* q_nope;          /* bf16 [num_tokens, num_heads, 128] */
+  int64_t q_nope_stride_t, q_nope_stride_h;
+  const void* q_pe;            /* bf16 [num_tokens, num_heads, 64] */
+  int64_t q_pe_stride_t, q_pe_stride_h;
+  const void* w_uk;            /* bf16 [num_heads, 128, 512] */
+  const void* kv_c;            /* bf16 [num_tokens, 512] */
+  int64_t kv_c_stride;
+  const void* k_pe;            /* bf16 [num_tokens, 64], before RoPE */
+  int64_t k_pe_stride;
+  const int64_t* positions;    /* [num_tokens] */
+  const float* cos_cache;      /* [max_position, 32] */
+  const float* sin_cache;      /* [max_position, 32] */
+  int64_t max_position;
+  const int64_t* slot_mapping; /* [num_tokens] */
+  void* kv_buffer;             /* uint8 [num_pages, 64, 384] */
+  void* kv_scales;             /* uint8 [num_pages, 64, 16]  */
+  int64_t num_pages;
+  void* q_out;                 /* bf16 [num_tokens, num_heads, 576] */
+  int64_t q_out_stride_t, q_out_stride_h;
+  int32_t num_tokens;
+  int32_t num_heads;
+  int32_t is_neox;
+  int32_t legacy_rule;
+} KimiQAbsorbParams;
+
+KIMI_API int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* params, void* stream);
+
 /* Row quantiser: x bf16 [rows, cols] (row stride x_stride elements, cols a
  * multiple of 32) -> nibbles uint8 [rows, cols/2] and scales uint8
  * [rows, cols/32], both contiguous. */

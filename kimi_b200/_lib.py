@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = (
     "kimi_mla_decode_static_workspace",
     "kimi_mla_decode_partial",
     "kimi_mla_decode_merge",
+    "kimi_mla_q_absorb_rope_append",
 )
 
 
@@ -81,6 +82,37 @@ class KimiKvAppendParams(ctypes.Structure):
     ]
 
 
+class KimiQAbsorbParams(ctypes.Structure):
+    _fields_ = [
+        ("q_nope", ctypes.c_void_p),
+        ("q_nope_stride_t", ctypes.c_int64),
+        ("q_nope_stride_h", ctypes.c_int64),
+        ("q_pe", ctypes.c_void_p),
+        ("q_pe_stride_t", ctypes.c_int64),
+        ("q_pe_stride_h", ctypes.c_int64),
+        ("w_uk", ctypes.c_void_p),
+        ("kv_c", ctypes.c_void_p),
+        ("kv_c_stride", ctypes.c_int64),
+        ("k_pe", ctypes.c_void_p),
+        ("k_pe_stride", ctypes.c_int64),
+        ("positions", ctypes.c_void_p),
+        ("cos_cache", ctypes.c_void_p),
+        ("sin_cache", ctypes.c_void_p),
+        ("max_position", ctypes.c_int64),
+        ("slot_mapping", ctypes.c_void_p),
+        ("kv_buffer", ctypes.c_void_p),
+        ("kv_scales", ctypes.c_void_p),
+        ("num_pages", ctypes.c_int64),
+        ("q_out", ctypes.c_void_p),
+        ("q_out_stride_t", ctypes.c_int64),
+        ("q_out_stride_h", ctypes.c_int64),
+        ("num_tokens", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("is_neox", ctypes.c_int32),
+        ("legacy_rule", ctypes.c_int32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -119,6 +151,8 @@ def load() -> ctypes.CDLL:
             fn.argtypes = [ctypes.POINTER(KimiMlaDecodeParams), vp, sz, vp]
         lib.kimi_mla_decode_static_workspace.restype = ctypes.c_int
         lib.kimi_mla_decode_static_workspace.argtypes = [ctypes.POINTER(KimiMlaDecodeParams), vp]
+        lib.kimi_mla_q_absorb_rope_append.restype = ctypes.c_int
+        lib.kimi_mla_q_absorb_rope_append.argtypes = [ctypes.POINTER(KimiQAbsorbParams), vp]
         lib.kimi_mxfp4_quantize.restype = ctypes.c_int
         lib.kimi_mxfp4_quantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, vp]
         _lib = lib

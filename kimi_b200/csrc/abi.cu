@@ -379,6 +379,57 @@ int kimi_mxfp4_kv_append(const KimiKvAppendParams* p, void* stream) {
   return cuda_status(kimi::launch_kv_append(a, static_cast<cudaStream_t>(stream)));
 }
 
+int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* p, void* stream) {
+  if (!p) return KIMI_ERR_NULL_POINTER;
+  if (p->num_tokens < 0 || p->num_heads < 1 || p->num_heads > KIMI_MLA_MAX_HEADS || p->num_pages < 0 ||
+      p->max_position < 1)
+    return KIMI_ERR_BAD_SHAPE;
+  if ((p->is_neox != 0 && p->is_neox != 1) || (p->legacy_rule != 0 && p->legacy_rule != 1))
+    return KIMI_ERR_UNSUPPORTED;
+  if (p->num_tokens == 0) return KIMI_OK;
+  if (!p->q_nope || !p->q_pe || !p->w_uk || !p->kv_c || !p->k_pe || !p->positions || !p->cos_cache ||
+      !p->sin_cache || !p->slot_mapping || !p->kv_buffer || !p->kv_scales || !p->q_out)
+    return KIMI_ERR_NULL_POINTER;
+  const int64_t strides[] = {p->q_nope_stride_t, p->q_nope_stride_h, p->q_pe_stride_t, p->q_pe_stride_h,
+                             p->kv_c_stride,     p->k_pe_stride,     p->q_out_stride_t, p->q_out_stride_h};
+  for (int64_t st : strides)
+    if (st % 8 || st < 0) return KIMI_ERR_BAD_STRIDE;
+  if (p->kv_c_stride < kLatent || p->k_pe_stride < 64) return KIMI_ERR_BAD_STRIDE;
+  if (!aligned(p->q_nope, 16) || !aligned(p->q_pe, 2) || !aligned(p->w_uk, 16) || !aligned(p->kv_c, 16) ||
+      !aligned(p->k_pe, 2) || !aligned(p->kv_buffer, 16) || !aligned(p->q_out, 16) ||
+      !aligned(p->positions, 8) || !aligned(p->slot_mapping, 8) || !aligned(p->cos_cache, 4) ||
+      !aligned(p->sin_cache, 4))
+    return KIMI_ERR_MISALIGNED;
+  kimi::QAbsorbArgs a;
+  a.q_nope = static_cast<const __nv_bfloat16*>(p->q_nope);
+  a.q_nope_stride_t = p->q_nope_stride_t;
+  a.q_nope_stride_h = p->q_nope_stride_h;
+  a.q_pe = static_cast<const __nv_bfloat16*>(p->q_pe);
+  a.q_pe_stride_t = p->q_pe_stride_t;
+  a.q_pe_stride_h = p->q_pe_stride_h;
+  a.w_uk = static_cast<const __nv_bfloat16*>(p->w_uk);
+  a.kv_c = static_cast<const __nv_bfloat16*>(p->kv_c);
+  a.kv_c_stride = p->kv_c_stride;
+  a.k_pe = static_cast<const __nv_bfloat16*>(p->k_pe);
+  a.k_pe_stride = p->k_pe_stride;
+  a.positions = p->positions;
+  a.cos = p->cos_cache;
+  a.sin = p->sin_cache;
+  a.max_position = p->max_position;
+  a.slot_mapping = p->slot_mapping;
+  a.kv_buffer = static_cast<uint8_t*>(p->kv_buffer);
+  a.kv_scales = static_cast<uint8_t*>(p->kv_scales);
+  a.num_pages = p->num_pages;
+  a.q_out = static_cast<__nv_bfloat16*>(p->q_out);
+  a.q_out_stride_t = p->q_out_stride_t;
+  a.q_out_stride_h = p->q_out_stride_h;
+  a.num_tokens = p->num_tokens;
+  a.num_heads = p->num_heads;
+  a.is_neox = p->is_neox;
+  a.legacy_rule = p->legacy_rule;
+  return cuda_status(kimi::launch_q_absorb(a, static_cast<cudaStream_t>(stream)));
+}
+
 int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,
                         int32_t legacy_rule, void* stream) {
   if (rows < 0 || cols < 0 || cols % 32) return KIMI_ERR_BAD_SHAPE;

@@ -42,6 +42,33 @@ struct KvAppendArgs {
   int legacy_rule;
 };
 
+// The decode prologue: q absorption by W_UK, RoPE of q_pe / k_pe, KV append.
+struct QAbsorbArgs {
+  const __nv_bfloat16* q_nope;  // [T, H, 128]
+  int64_t q_nope_stride_t, q_nope_stride_h;
+  const __nv_bfloat16* q_pe;    // [T, H, 64]
+  int64_t q_pe_stride_t, q_pe_stride_h;
+  const __nv_bfloat16* w_uk;    // [H, 128, 512] contiguous
+  const __nv_bfloat16* kv_c;    // [T, 512]
+  int64_t kv_c_stride;
+  const __nv_bfloat16* k_pe;    // [T, 64], before RoPE
+  int64_t k_pe_stride;
+  const int64_t* positions;     // [T]
+  const float* cos;             // [max_position, 32]
+  const float* sin;             // [max_position, 32]
+  int64_t max_position;
+  const int64_t* slot_mapping;  // [T]
+  uint8_t* kv_buffer;
+  uint8_t* kv_scales;
+  int64_t num_pages;
+  __nv_bfloat16* q_out;         // [T, H, 576]
+  int64_t q_out_stride_t, q_out_stride_h;
+  int num_tokens;
+  int num_heads;
+  int is_neox;
+  int legacy_rule;
+};
+
 struct QuantizeArgs {
   const __nv_bfloat16* x;
   int64_t rows;
@@ -113,6 +140,7 @@ struct ReduceArgs {
 };
 
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);
+cudaError_t launch_q_absorb(const QAbsorbArgs& a, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream);

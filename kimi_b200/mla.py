@@ -252,6 +252,68 @@ def mxfp4_kv_append(kv_c: torch.Tensor, k_pe: torch.Tensor, kv_buffer: torch.Ten
     _lib.check(status, "kimi_mxfp4_kv_append")
 
 
+def q_absorb_rope_append(q_nope: torch.Tensor, q_pe: torch.Tensor, w_uk: torch.Tensor, kv_c: torch.Tensor,
+                         k_pe: torch.Tensor, positions: torch.Tensor, cos_cache: torch.Tensor,
+                         sin_cache: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Tensor,
+                         slot_mapping: torch.Tensor, q_out: torch.Tensor | None = None, is_neox: bool = False,
+                         legacy_rule: bool = False) -> torch.Tensor:
+    """The decode step before attention in one launch (the reference's
+    ``fused_kv_bmm``, patches/atom-optimizations.patch:468-639):
+
+    * ``q_out[t, h, :512] = q_nope[t, h] @ w_uk[h]`` (q absorbed by W_UK);
+    * ``q_out[t, h, 512:] = rope(q_pe[t, h], positions[t])``;
+    * the cache gets MXFP4(``kv_c[t]``) and ``rope(k_pe[t], positions[t])``
+      at ``slot_mapping[t]``.
+
+    Shapes: q_nope bf16 [T, H, 128], q_pe bf16 [T, H, 64] (both may be views
+    of one [T, H, 192] projection), w_uk bf16 [H, 128, 512] contiguous, kv_c
+    bf16 [T, 512], k_pe bf16 [T, 64] before RoPE, positions int64 [T],
+    cos_cache / sin_cache float32 [max_position, 32], slot_mapping int64
+    [T].  ``q_out`` (bf16 [T, H, 576], allocated when None) is returned and is
+    the decode's ``q``.  ``is_neox`` selects the rotary pairing
+    (x[i], x[i+32]) instead of (x[2i], x[2i+1]).
+    """
+    dev = _require_cuda(q_nope, q_pe, w_uk, kv_c, k_pe, positions, cos_cache, sin_cache, kv_buffer, kv_scales,
+                        slot_mapping)
+    num_pages = _cache_views(kv_buffer, kv_scales)
+    for name, t in (("q_nope", q_nope), ("q_pe", q_pe), ("w_uk", w_uk), ("kv_c", kv_c), ("k_pe", k_pe)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bfloat16")
+    if q_nope.dim() != 3 or q_nope.shape[2] != 128 or q_nope.stride(2) != 1:
+        raise ValueError("q_nope must be [T, H, 128] with a contiguous last dim")
+    T, H = q_nope.shape[0], q_nope.shape[1]
+    if q_pe.shape != (T, H, ROPE_DIM) or q_pe.stride(2) != 1:
+        raise ValueError("q_pe must be [T, H, 64] with a contiguous last dim")
+    if w_uk.shape != (H, 128, KV_LORA_RANK) or not w_uk.is_contiguous():
+        raise ValueError("w_uk must be a contiguous [H, 128, 512] tensor")
+    if kv_c.shape != (T, KV_LORA_RANK) or kv_c.stride(1) != 1 or k_pe.shape != (T, ROPE_DIM) or k_pe.stride(1) != 1:
+        raise ValueError("kv_c must be [T, 512] and k_pe [T, 64], contiguous in the last dim")
+    for name, t in (("positions", positions), ("slot_mapping", slot_mapping)):
+        if t.dtype != torch.int64 or t.numel() != T or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous int64 tensor with T entries")
+    if (cos_cache.dtype != torch.float32 or sin_cache.dtype != torch.float32 or cos_cache.dim() != 2
+            or cos_cache.shape[1] != 32 or sin_cache.shape != cos_cache.shape or not cos_cache.is_contiguous()
+            or not sin_cache.is_contiguous()):
+        raise ValueError("cos_cache and sin_cache must be contiguous float32 [max_position, 32]")
+    if q_out is None:
+        q_out = torch.empty(T, H, QK_DIM, dtype=torch.bfloat16, device=dev)
+    if q_out.dtype != torch.bfloat16 or q_out.shape != (T, H, QK_DIM) or q_out.stride(2) != 1:
+        raise ValueError("q_out must be a bf16 [T, H, 576] tensor with a contiguous last dim")
+    p = _lib.KimiQAbsorbParams(
+        q_nope=q_nope.data_ptr(), q_nope_stride_t=q_nope.stride(0), q_nope_stride_h=q_nope.stride(1),
+        q_pe=q_pe.data_ptr(), q_pe_stride_t=q_pe.stride(0), q_pe_stride_h=q_pe.stride(1), w_uk=w_uk.data_ptr(),
+        kv_c=kv_c.data_ptr(), kv_c_stride=kv_c.stride(0), k_pe=k_pe.data_ptr(), k_pe_stride=k_pe.stride(0),
+        positions=positions.data_ptr(), cos_cache=cos_cache.data_ptr(), sin_cache=sin_cache.data_ptr(),
+        max_position=cos_cache.shape[0], slot_mapping=slot_mapping.data_ptr(), kv_buffer=kv_buffer.data_ptr(),
+        kv_scales=kv_scales.data_ptr(), num_pages=num_pages, q_out=q_out.data_ptr(),
+        q_out_stride_t=q_out.stride(0), q_out_stride_h=q_out.stride(1), num_tokens=T, num_heads=H,
+        is_neox=int(bool(is_neox)), legacy_rule=int(bool(legacy_rule)))
+    with torch.cuda.device(dev):
+        status = _lib.load().kimi_mla_q_absorb_rope_append(ctypes.byref(p), _stream_handle(dev))
+    _lib.check(status, "kimi_mla_q_absorb_rope_append")
+    return q_out
+
+
 def mxfp4_quantize(x: torch.Tensor, legacy_rule: bool = False):
     """bf16 [rows, cols] (cols % 32 == 0) -> (nibbles u8 [rows, cols/2], scales u8 [rows, cols/32])."""
     dev = _require_cuda(x)

@@ -9,13 +9,18 @@ library's KV-append quantiser).  A step is one decode call over the whole
 batch (one layer).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload kimi_k2|ragged]
+                    [--workload kimi_k2|ragged|tp8_prologue]
 
 ``--workload ragged`` runs the batch-sharded sweep instead: one batch of 256
 sequences with lengths drawn uniformly from 1K-32K tokens (seeded), spread
 over the N ranks by longest-first bin packing (kimi_b200.dp), each rank
 holding only its sequences' pages; the whole batch is fixed as N grows
 (strong scaling) and the gather of the outputs to rank 0 is timed separately.
+
+``--workload tp8_prologue`` times the decode step before attention instead:
+q absorption by W_UK + RoPE + MXFP4 KV append (kimi_b200.q_absorb_rope_append)
+at the Kimi-K2 TP8 shape per GPU (8 heads, 128 tokens), in microseconds per
+call, next to the same step as separate torch / library calls.
 
 Prints one JSON line on rank 0.  ``value`` is the aggregate achieved HBM
 bandwidth over all ranks computed from the algorithmic bytes (latent nibbles
@@ -443,13 +448,134 @@ def run_reference(args, rank):
     }
 
 
+# ---------------------------------------------------------------------------
+# the decode prologue (q absorb + RoPE + MXFP4 KV append), Kimi-K2 TP8 shape
+# ---------------------------------------------------------------------------
+PRO_TOKENS, PRO_HEADS, PRO_MAXPOS, PRO_SETS = 128, 8, 8192, 64
+
+
+def prologue_bytes(T=PRO_TOKENS, H=PRO_HEADS) -> int:
+    """Algorithmic bytes of one call: q (nope + pe), W_UK, kv_c + k_pe,
+    positions / slots, the cos / sin rows, q_out and the cache rows written."""
+    return (T * H * 192 * 2 + H * 128 * 512 * 2 + T * 576 * 2 + T * 16 + T * 2 * 32 * 4
+            + T * H * 576 * 2 + T * 400)
+
+
+def run_prologue(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import kimi_b200 as kimi
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T, H = PRO_TOKENS, PRO_HEADS
+    g = torch.Generator(device=dev).manual_seed(5 + 1000 * rank)
+    bf = torch.bfloat16
+    freqs = 1.0 / (10000.0 ** (torch.arange(32, device=dev, dtype=torch.float64) / 32.0))
+    ang = torch.arange(PRO_MAXPOS, device=dev, dtype=torch.float64)[:, None] * freqs[None, :]
+    cos, sin = ang.cos().float().contiguous(), ang.sin().float().contiguous()
+    kvb, kvs = kimi.alloc_mxfp4_cache(PRO_SETS * T // 64, dev)
+    # PRO_SETS independent call inputs (~180 MB in all, more than the 126 MB L2), used in turn
+    sets = []
+    for i in range(PRO_SETS):
+        sets.append(dict(
+            q=torch.randn(T, H, 192, generator=g, device=dev).to(bf),
+            w=(torch.randn(H, 128, 512, generator=g, device=dev) / math.sqrt(128.0)).to(bf),
+            kv_c=torch.randn(T, 512, generator=g, device=dev).to(bf),
+            k_pe=torch.randn(T, 64, generator=g, device=dev).to(bf),
+            pos=torch.randint(0, PRO_MAXPOS, (T,), generator=g, device=dev),
+            slots=torch.arange(i * T, (i + 1) * T, device=dev, dtype=torch.int64),
+            out=torch.empty(T, H, 576, dtype=bf, device=dev)))
+
+    def fused(i):
+        s_ = sets[i % PRO_SETS]
+        kimi.q_absorb_rope_append(s_["q"][:, :, :128], s_["q"][:, :, 128:], s_["w"], s_["kv_c"], s_["k_pe"],
+                                  s_["pos"], cos, sin, kvb, kvs, s_["slots"], q_out=s_["out"])
+
+    def rope_torch(x, pos):  # (x[2i], x[2i+1]) pairs, float32
+        c, sn = cos[pos], sin[pos]
+        while c.dim() < x.dim():
+            c, sn = c.unsqueeze(-2), sn.unsqueeze(-2)
+        xf = x.float()
+        a, b = xf[..., 0::2], xf[..., 1::2]
+        return torch.stack((a * c - b * sn, b * c + a * sn), dim=-1).flatten(-2).to(bf)
+
+    def unfused(i):  # the same step as separate library / torch calls
+        s_ = sets[i % PRO_SETS]
+        out = s_["out"]
+        out[:, :, :512] = torch.bmm(s_["q"][:, :, :128].transpose(0, 1), s_["w"]).transpose(0, 1)
+        out[:, :, 512:] = rope_torch(s_["q"][:, :, 128:], s_["pos"])
+        kimi.mxfp4_kv_append(s_["kv_c"], rope_torch(s_["k_pe"], s_["pos"]), kvb, kvs, s_["slots"])
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        # Both paths are captured into a CUDA graph of PRO_SETS calls and the
+        # graph is replayed: the host's per-call Python and launch overhead
+        # (tens of microseconds) would otherwise set the pace, not the GPU.
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(PRO_SETS):
+                fn(i)
+        reps = max(1, args.steps // PRO_SETS)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * PRO_SETS)
+        del graph
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with ClockSampler(dev.index) as clocks:
+        ms = timed(fused)
+    ms_unfused = timed(unfused)
+    if rank != 0:
+        return None
+    peak, peak_kind = _peak_hbm()
+    nbytes = prologue_bytes()
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": "decode prologue latency (q absorb by W_UK + RoPE + MXFP4 KV append), Kimi-K2 TP8 per GPU",
+        "value": round(ms * 1e3, 3), "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 6), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded normal q, W_UK ~ N(0, 1/128), latents; random positions)",
+        "config": {"workload": f"Kimi-K2 TP8 decode prologue: {H} heads per GPU, {T} tokens, W_UK [{H}, 128, 512], "
+                               f"RoPE table {PRO_MAXPOS} positions (GPT-J pairing), cache page 64",
+                   "l2": f"inputs larger than L2: {PRO_SETS} independent input sets used in turn",
+                   "parallelism": f"{world} replica(s), one per GPU, no collective"},
+        "gpu_launches": max(1, args.steps // PRO_SETS) * PRO_SETS,
+        "timing": "CUDA graph of 64 calls replayed; device time per call",
+        "unfused_us": round(ms_unfused * 1e3, 3),
+        "unfused_path": "torch.bmm + torch RoPE + kimi_b200.mxfp4_kv_append (same results, several launches)",
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "note": f"{nbytes} algorithmic bytes per call; launch- and latency-bound at this size"},
+        "clocks": clocks.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["kimi_k2", "ragged"], default="kimi_k2")
+    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "tp8_prologue"], default="kimi_k2")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
                     help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
     args = ap.parse_args()
@@ -473,7 +599,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = run_ours(args, rank, world, local_rank)
+        line = (run_prologue if args.workload == "tp8_prologue" else run_ours)(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -395,10 +395,10 @@ int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* p, void* stream) {
   for (int64_t st : strides)
     if (st % 8 || st < 0) return KIMI_ERR_BAD_STRIDE;
   if (p->kv_c_stride < kLatent || p->k_pe_stride < 64) return KIMI_ERR_BAD_STRIDE;
-  if (!aligned(p->q_nope, 16) || !aligned(p->q_pe, 2) || !aligned(p->w_uk, 16) || !aligned(p->kv_c, 16) ||
+  if (!aligned(p->q_nope, 16) || !aligned(p->q_pe, 16) || !aligned(p->w_uk, 16) || !aligned(p->kv_c, 16) ||
       !aligned(p->k_pe, 2) || !aligned(p->kv_buffer, 16) || !aligned(p->q_out, 16) ||
-      !aligned(p->positions, 8) || !aligned(p->slot_mapping, 8) || !aligned(p->cos_cache, 4) ||
-      !aligned(p->sin_cache, 4))
+      !aligned(p->positions, 8) || !aligned(p->slot_mapping, 8) || !aligned(p->cos_cache, 16) ||
+      !aligned(p->sin_cache, 16))
     return KIMI_ERR_MISALIGNED;
   kimi::QAbsorbArgs a;
   a.q_nope = static_cast<const __nv_bfloat16*>(p->q_nope);

@@ -240,6 +240,36 @@ typedef struct KimiQAbsorbParams {
 
 KIMI_API int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* params, void* stream);
 
+/* The layer-input step after the tensor-parallel all-reduce, in one kernel.
+ * Replaces the fused one-shot all-reduce + residual + RMSNorm
+ * (`allreduce_fusion_kernel_1stage_nloop`, patches/aiter-1stage-nloop-ar-rmsnorm.patch:12-253)
+ * and the MXFP4 quant-only step after it (patches/aiter-mxfp4-quant-only.patch:29-125):
+ *   residual_out = bf16(inputs[0] + ... + inputs[n-1] + residual)   (float32 sum, rank order)
+ *   out          = bf16(bf16(residual_out * rsqrt(mean(residual_out^2) + eps)) * weight)
+ *   nibbles / scales = MXFP4(out), scales unshuffled [rows, hidden / 32].
+ * inputs[] are the ranks' partial outputs, each bf16 [rows, hidden]
+ * contiguous: device pointers this GPU can read (its own buffer and peer
+ * buffers mapped over NVLink).  The caller orders the call after every
+ * partial is written and keeps the partials unchanged until every rank's call
+ * has finished (the call itself waits for nothing).  hidden: a multiple of 32,
+ * at most 32768.  residual_out may alias residual. */
+#define KIMI_AR_MAX_INPUTS 8
+typedef struct KimiArRmsNormParams {
+  const void* inputs[KIMI_AR_MAX_INPUTS]; /* bf16 [rows, hidden] each */
+  int32_t num_inputs;
+  const void* residual;        /* bf16 [rows, hidden] */
+  void* residual_out;          /* bf16 [rows, hidden] */
+  const void* weight;          /* bf16 [hidden] */
+  float eps;
+  void* nibbles;               /* uint8 [rows, hidden / 2] */
+  void* scales;                /* uint8 [rows, hidden / 32] */
+  int32_t rows;
+  int32_t hidden;
+  int32_t legacy_rule;
+} KimiArRmsNormParams;
+
+KIMI_API int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* params, void* stream);
+
 /* Row quantiser: x bf16 [rows, cols] (row stride x_stride elements, cols a
  * multiple of 32) -> nibbles uint8 [rows, cols/2] and scales uint8
  * [rows, cols/32], both contiguous. */

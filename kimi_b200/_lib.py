@@ -29,7 +29,10 @@ EXPORTED_SYMBOLS = (
     "kimi_mla_decode_partial",
     "kimi_mla_decode_merge",
     "kimi_mla_q_absorb_rope_append",
+    "kimi_ar_rmsnorm_mxfp4",
 )
+
+AR_MAX_INPUTS = 8
 
 
 class KimiMlaDecodeParams(ctypes.Structure):
@@ -113,6 +116,22 @@ class KimiQAbsorbParams(ctypes.Structure):
     ]
 
 
+class KimiArRmsNormParams(ctypes.Structure):
+    _fields_ = [
+        ("inputs", ctypes.c_void_p * 8),
+        ("num_inputs", ctypes.c_int32),
+        ("residual", ctypes.c_void_p),
+        ("residual_out", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+        ("nibbles", ctypes.c_void_p),
+        ("scales", ctypes.c_void_p),
+        ("rows", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("legacy_rule", ctypes.c_int32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -153,6 +172,8 @@ def load() -> ctypes.CDLL:
         lib.kimi_mla_decode_static_workspace.argtypes = [ctypes.POINTER(KimiMlaDecodeParams), vp]
         lib.kimi_mla_q_absorb_rope_append.restype = ctypes.c_int
         lib.kimi_mla_q_absorb_rope_append.argtypes = [ctypes.POINTER(KimiQAbsorbParams), vp]
+        lib.kimi_ar_rmsnorm_mxfp4.restype = ctypes.c_int
+        lib.kimi_ar_rmsnorm_mxfp4.argtypes = [ctypes.POINTER(KimiArRmsNormParams), vp]
         lib.kimi_mxfp4_quantize.restype = ctypes.c_int
         lib.kimi_mxfp4_quantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, vp]
         _lib = lib

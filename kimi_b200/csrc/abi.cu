@@ -430,6 +430,37 @@ int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* p, void* stream) {
   return cuda_status(kimi::launch_q_absorb(a, static_cast<cudaStream_t>(stream)));
 }
 
+int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* p, void* stream) {
+  if (!p) return KIMI_ERR_NULL_POINTER;
+  if (p->rows < 0 || p->hidden < 32 || p->hidden % 32 || p->hidden > 32768 || p->num_inputs < 1 ||
+      p->num_inputs > KIMI_AR_MAX_INPUTS || !std::isfinite(p->eps) || p->eps < 0.f)
+    return KIMI_ERR_BAD_SHAPE;
+  if (p->legacy_rule != 0 && p->legacy_rule != 1) return KIMI_ERR_UNSUPPORTED;
+  if (p->rows == 0) return KIMI_OK;
+  if (!p->residual || !p->residual_out || !p->weight || !p->nibbles || !p->scales) return KIMI_ERR_NULL_POINTER;
+  kimi::ArNormArgs a;
+  for (int i = 0; i < p->num_inputs; ++i) {
+    if (!p->inputs[i]) return KIMI_ERR_NULL_POINTER;
+    if (!aligned(p->inputs[i], 16)) return KIMI_ERR_MISALIGNED;
+    a.inputs[i] = static_cast<const __nv_bfloat16*>(p->inputs[i]);
+  }
+  for (int i = p->num_inputs; i < kimi::kArMaxInputs; ++i) a.inputs[i] = nullptr;
+  if (!aligned(p->residual, 16) || !aligned(p->residual_out, 16) || !aligned(p->weight, 16) ||
+      !aligned(p->nibbles, 16))
+    return KIMI_ERR_MISALIGNED;
+  a.num_inputs = p->num_inputs;
+  a.residual = static_cast<const __nv_bfloat16*>(p->residual);
+  a.residual_out = static_cast<__nv_bfloat16*>(p->residual_out);
+  a.weight = static_cast<const __nv_bfloat16*>(p->weight);
+  a.eps = p->eps;
+  a.nibbles = static_cast<uint8_t*>(p->nibbles);
+  a.scales = static_cast<uint8_t*>(p->scales);
+  a.rows = p->rows;
+  a.hidden = p->hidden;
+  a.legacy_rule = p->legacy_rule;
+  return cuda_status(kimi::launch_ar_norm_quant(a, static_cast<cudaStream_t>(stream)));
+}
+
 int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,
                         int32_t legacy_rule, void* stream) {
   if (rows < 0 || cols < 0 || cols % 32) return KIMI_ERR_BAD_SHAPE;

@@ -1,0 +1,130 @@
+// The layer-input step after the tensor-parallel all-reduce, in one kernel:
+// the ranks' partial hidden states summed (read straight from each rank's
+// buffer: peer pointers over NVLink, or local buffers), the residual added and
+// written back, RMSNorm with its weight, MXFP4 quantisation.
+//
+// Reference (paths inside ianye23301/kimi): the one-shot fused all-reduce +
+// residual + RMSNorm `allreduce_fusion_kernel_1stage_nloop`
+// (patches/aiter-1stage-nloop-ar-rmsnorm.patch:12-253) and the MXFP4
+// quant-only step after it (patches/aiter-mxfp4-quant-only.patch:29-125;
+// checked against the fused norm+quant in tests/test_ar_fusion_correctness.py:15-151):
+//   combined = bf16(sum_r x_r + residual)            -> residual_out
+//   normed   = bf16(combined * rsqrt(mean(combined^2) + eps))
+//   out      = bf16(normed * weight)                 -> MXFP4 (unshuffled scales)
+//
+// One CTA per row; thread g owns elements 32 g .. 32 g + 31 -- exactly one
+// MXFP4 group -- so the only cross-thread step is the sum of squares: the
+// thread's 32 squares in order, a warp butterfly (lane 0's value kept), the
+// warps in order.  Every float32 step is the oracle's, so the results are
+// bit-exact.  Loads and stores are 16-byte vectors; the kernel is one pass
+// over the inputs (bound by HBM or, for peer inputs, by NVLink).
+//
+// The caller orders the kernel after every rank's partial is complete and
+// keeps each partial unchanged until every rank's kernel has read it (for
+// example with a stream-ordered barrier on both sides); the kernel itself
+// waits for nothing.
+#include <cuda_runtime.h>
+
+#include "kernels.cuh"
+#include "mxfp4.cuh"
+
+namespace kimi {
+namespace {
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float* x) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    x[2 * j] = __uint_as_float(w[j] << 16);
+    x[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+template <bool LEGACY>
+__global__ void __launch_bounds__(1024) ar_norm_quant_kernel(const __grid_constant__ ArNormArgs a) {
+  __shared__ float warp_sum[32];
+  __shared__ float rstd;
+  const int row = blockIdx.x, g = threadIdx.x, lane = g & 31, warp = g >> 5;
+  const int groups = a.hidden / 32;
+  const bool live = g < groups;
+  const int64_t off = static_cast<int64_t>(row) * a.hidden + 32 * g;
+
+  float c[32];
+  float sq = 0.f;
+  if (live) {
+    float acc[32], t[8];
+    // sum over the ranks in rank order, then the residual
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(a.inputs[0] + off)[p], acc + 8 * p);
+    }
+    for (int r = 1; r < a.num_inputs; ++r) {
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        bf16x8_to_f32(reinterpret_cast<const uint4*>(a.inputs[r] + off)[p], t);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[8 * p + j] = __fadd_rn(acc[8 * p + j], t[j]);
+      }
+    }
+    uint32_t packed[16];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(a.residual + off)[p], t);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) c[8 * p + j] = round_bf16(__fadd_rn(acc[8 * p + j], t[j]));
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const __nv_bfloat162 pr = __floats2bfloat162_rn(c[2 * j], c[2 * j + 1]);
+      packed[j] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    uint4* ro = reinterpret_cast<uint4*>(a.residual_out + off);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) ro[p] = make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sq = __fadd_rn(sq, __fmul_rn(c[i], c[i]));
+  }
+  // warp butterfly (lane 0's value), then the warps in order
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+  if (lane == 0) warp_sum[warp] = sq;
+  __syncthreads();
+  if (g == 0) {
+    float total = 0.f;
+    for (int w = 0; w < (blockDim.x >> 5); ++w) total = __fadd_rn(total, warp_sum[w]);
+    const float var = __fdiv_rn(total, static_cast<float>(a.hidden));
+    rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+  }
+  __syncthreads();
+  if (!live) return;
+  const float r = rstd;
+  float out[32];
+  float wt[8];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(a.weight + 32 * g)[p], wt);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[8 * p + j] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(c[8 * p + j], r)), wt[j]));
+  }
+  uint32_t nib[4];
+  uint8_t sb;
+  quantize_group32<LEGACY>(out, nib, sb);
+  *reinterpret_cast<uint4*>(a.nibbles + static_cast<int64_t>(row) * (a.hidden / 2) + 16 * g) =
+      make_uint4(nib[0], nib[1], nib[2], nib[3]);
+  a.scales[static_cast<int64_t>(row) * groups + g] = sb;
+}
+
+}  // namespace
+
+cudaError_t launch_ar_norm_quant(const ArNormArgs& a, cudaStream_t stream) {
+  const int threads = ((a.hidden / 32) + 31) / 32 * 32;
+  if (a.legacy_rule)
+    ar_norm_quant_kernel<true><<<a.rows, threads, 0, stream>>>(a);
+  else
+    ar_norm_quant_kernel<false><<<a.rows, threads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace kimi

@@ -69,6 +69,22 @@ struct QAbsorbArgs {
   int legacy_rule;
 };
 
+// Sum of the ranks' partial rows + residual, RMSNorm, MXFP4 (one CTA per row).
+constexpr int kArMaxInputs = 8;
+struct ArNormArgs {
+  const __nv_bfloat16* inputs[kArMaxInputs];  // [rows, hidden] each, rank order
+  int num_inputs;
+  const __nv_bfloat16* residual;              // [rows, hidden]
+  __nv_bfloat16* residual_out;                // [rows, hidden] (may alias residual)
+  const __nv_bfloat16* weight;                // [hidden]
+  float eps;
+  uint8_t* nibbles;                           // [rows, hidden / 2]
+  uint8_t* scales;                            // [rows, hidden / 32]
+  int rows;
+  int hidden;
+  int legacy_rule;
+};
+
 struct QuantizeArgs {
   const __nv_bfloat16* x;
   int64_t rows;
@@ -141,6 +157,7 @@ struct ReduceArgs {
 
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);
 cudaError_t launch_q_absorb(const QAbsorbArgs& a, cudaStream_t stream);
+cudaError_t launch_ar_norm_quant(const ArNormArgs& a, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream);

@@ -9,7 +9,7 @@ library's KV-append quantiser).  A step is one decode call over the whole
 batch (one layer).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload kimi_k2|ragged|tp8_prologue]
+                    [--workload kimi_k2|ragged|tp8_prologue|tp8_ar_norm]
 
 ``--workload ragged`` runs the batch-sharded sweep instead: one batch of 256
 sequences with lengths drawn uniformly from 1K-32K tokens (seeded), spread
@@ -21,6 +21,10 @@ holding only its sequences' pages; the whole batch is fixed as N grows
 q absorption by W_UK + RoPE + MXFP4 KV append (kimi_b200.q_absorb_rope_append)
 at the Kimi-K2 TP8 shape per GPU (8 heads, 128 tokens), in microseconds per
 call, next to the same step as separate torch / library calls.
+``--workload tp8_ar_norm`` times the layer-input step after the TP8
+all-reduce (kimi_b200.tp: 8 partials + residual + RMSNorm + MXFP4): on one GPU
+with 8 local buffers standing in for the ranks, under torchrun with every
+rank's real buffer read over NVLink.
 
 Prints one JSON line on rank 0.  ``value`` is the aggregate achieved HBM
 bandwidth over all ranks computed from the algorithmic bytes (latent nibbles
@@ -569,13 +573,132 @@ def run_prologue(args, rank, world, local_rank):
     }
 
 
+# ---------------------------------------------------------------------------
+# the layer-input step after the TP8 all-reduce: sum of 8 partials + residual +
+# RMSNorm + MXFP4, Kimi-K2 hidden 7168, 128 tokens
+# ---------------------------------------------------------------------------
+AR_ROWS, AR_HIDDEN, AR_RANKS, AR_SETS = 128, 7168, 8, 8
+
+
+def run_ar_norm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import kimi_b200 as kimi
+    from kimi_b200 import tp
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(9 + rank)
+    bf = torch.bfloat16
+    rows, hidden = AR_ROWS, AR_HIDDEN
+    weight = torch.randn(hidden, generator=g, device=dev).to(bf)
+    if world > 1:
+        # the ranks' real partial buffers, read over NVLink
+        peers = tp.PeerPartials(rows, hidden, dev)
+        peers.local.copy_(torch.randn(rows, hidden, generator=g, device=dev).to(bf))
+        sets = [dict(inputs=peers.buffers, res=torch.randn(rows, hidden, generator=g, device=dev).to(bf))
+                for _ in range(AR_SETS)]
+        ranks = world
+    else:
+        # one GPU: the 8 ranks' partials as 8 local buffers per input set (the same
+        # bytes per call, from HBM instead of over NVLink)
+        sets = [dict(inputs=[torch.randn(rows, hidden, generator=g, device=dev).to(bf) for _ in range(AR_RANKS)],
+                     res=torch.randn(rows, hidden, generator=g, device=dev).to(bf)) for _ in range(AR_SETS)]
+        ranks = AR_RANKS
+    outs = [dict(r=torch.empty(rows, hidden, dtype=bf, device=dev),
+                 n=torch.empty(rows, hidden // 2, dtype=torch.uint8, device=dev),
+                 s=torch.empty(rows, hidden // 32, dtype=torch.uint8, device=dev)) for _ in range(AR_SETS)]
+
+    def fused(i):
+        st, o = sets[i % AR_SETS], outs[i % AR_SETS]
+        tp.ar_rmsnorm_mxfp4(st["inputs"], st["res"], weight, 1e-6, residual_out=o["r"], nibbles=o["n"], scales=o["s"])
+
+    def unfused(i):  # the same arithmetic as separate torch / library calls (the all-reduce as a sum on one GPU)
+        st = sets[i % AR_SETS]
+        acc = st["inputs"][0].float()
+        for x in st["inputs"][1:]:
+            acc = acc + x.float()
+        comb = (acc + st["res"].float()).to(bf)
+        normed = (comb.float() * torch.rsqrt(comb.float().pow(2).mean(-1, keepdim=True) + 1e-6)).to(bf) * weight
+        kimi.mxfp4_quantize(normed)
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, graphed):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        if graphed:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(AR_SETS):
+                    fn(i)
+            run = graph.replay
+            per = AR_SETS
+        else:
+            run, per = (lambda: fn(0)), 1
+        reps = max(1, args.steps // per)
+        run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * per)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # with peers the kernel runs between the callers' barriers; only the kernel is timed here
+    with ClockSampler(dev.index) as clocks:
+        ms = timed(fused, graphed=True)
+    ms_unfused = timed(unfused, graphed=True) if world == 1 else None
+    if world > 1:
+        del sets, peers
+    if rank != 0:
+        return None
+    peak, peak_kind = _peak_hbm()
+    nbytes = rows * hidden * 2 * (ranks + 2) + rows * hidden // 2 + rows * hidden // 32 + hidden * 2
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "TP8 layer-input step (all-reduce of 8 partials + residual + RMSNorm + MXFP4), Kimi-K2 hidden 7168",
+        "value": round(ms * 1e3, 3), "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 6), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded normal partials, residual and weight)",
+        "config": {"workload": f"{rows} tokens x hidden {hidden}, {ranks} partials summed, eps 1e-6, "
+                               "MXFP4 inline rule, unshuffled scales",
+                   "partials": "peer buffers over NVLink" if world > 1 else
+                               f"{AR_RANKS} local buffers standing in for the {AR_RANKS} ranks",
+                   "l2": f"{AR_SETS} input sets used in turn",
+                   "timing": "CUDA graph of the kernel calls replayed; device time per call"},
+        "gpu_launches": max(1, args.steps // AR_SETS) * AR_SETS,
+        "roofline": {"bound": "hbm" if world == 1 else "nvlink", "achieved": round(achieved, 1),
+                     "peak": peak if world == 1 else 770.0 * (ranks - 1) / ranks * ranks,
+                     "unit": "GB/s", "frac": None, "traffic": None,
+                     "note": f"{nbytes} algorithmic bytes per call"},
+        "clocks": clocks.summary(),
+    }
+    line["roofline"]["frac"] = round(achieved / line["roofline"]["peak"], 4)
+    if ms_unfused is not None:
+        line["unfused_us"] = round(ms_unfused * 1e3, 3)
+        line["unfused_path"] = "torch sum + add + RMSNorm + kimi_b200.mxfp4_quantize (same arithmetic)"
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "tp8_prologue"], default="kimi_k2")
+    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "tp8_prologue", "tp8_ar_norm"], default="kimi_k2")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
                     help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
     args = ap.parse_args()
@@ -599,7 +722,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = (run_prologue if args.workload == "tp8_prologue" else run_ours)(args, rank, world, local_rank)
+        runner = {"tp8_prologue": run_prologue, "tp8_ar_norm": run_ar_norm}.get(args.workload, run_ours)
+        line = runner(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -252,7 +252,7 @@ KIMI_API int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* params, void
  * buffers mapped over NVLink).  The caller orders the call after every
  * partial is written and keeps the partials unchanged until every rank's call
  * has finished (the call itself waits for nothing).  hidden: a multiple of 32,
- * at most 32768.  residual_out may alias residual. */
+ * at most 8192.  residual_out may alias residual. */
 #define KIMI_AR_MAX_INPUTS 8
 typedef struct KimiArRmsNormParams {
   const void* inputs[KIMI_AR_MAX_INPUTS]; /* bf16 [rows, hidden] each */

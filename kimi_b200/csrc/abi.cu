@@ -432,7 +432,7 @@ int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* p, void* stream) {
 
 int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* p, void* stream) {
   if (!p) return KIMI_ERR_NULL_POINTER;
-  if (p->rows < 0 || p->hidden < 32 || p->hidden % 32 || p->hidden > 32768 || p->num_inputs < 1 ||
+  if (p->rows < 0 || p->hidden < 32 || p->hidden % 32 || p->hidden > 8192 || p->num_inputs < 1 ||
       p->num_inputs > KIMI_AR_MAX_INPUTS || !std::isfinite(p->eps) || p->eps < 0.f)
     return KIMI_ERR_BAD_SHAPE;
   if (p->legacy_rule != 0 && p->legacy_rule != 1) return KIMI_ERR_UNSUPPORTED;

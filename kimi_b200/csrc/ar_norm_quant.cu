@@ -43,7 +43,7 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float* x) {
 __device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 template <bool LEGACY>
-__global__ void __launch_bounds__(1024) ar_norm_quant_kernel(const __grid_constant__ ArNormArgs a) {
+__global__ void __launch_bounds__(256) ar_norm_quant_kernel(const __grid_constant__ ArNormArgs a) {
   __shared__ float warp_sum[32];
   __shared__ float rstd;
   const int row = blockIdx.x, g = threadIdx.x, lane = g & 31, warp = g >> 5;
@@ -53,25 +53,38 @@ __global__ void __launch_bounds__(1024) ar_norm_quant_kernel(const __grid_consta
 
   float c[32];
   float sq = 0.f;
+  uint4 wraw[4];  // the weight's 64 bytes, loaded with the partials
   if (live) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) wraw[p] = reinterpret_cast<const uint4*>(a.weight + 32 * g)[p];
     float acc[32], t[8];
-    // sum over the ranks in rank order, then the residual
+    // every rank's 64 bytes and the residual's are loaded first (all in
+    // flight together), then summed in rank order, then the residual added
+    uint4 raw[kArMaxInputs][4], rres[4];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      bf16x8_to_f32(reinterpret_cast<const uint4*>(a.inputs[0] + off)[p], acc + 8 * p);
-    }
-    for (int r = 1; r < a.num_inputs; ++r) {
+    for (int r = 0; r < kArMaxInputs; ++r)
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        bf16x8_to_f32(reinterpret_cast<const uint4*>(a.inputs[r] + off)[p], t);
+      for (int p = 0; p < 4; ++p)
+        raw[r][p] = r < a.num_inputs ? reinterpret_cast<const uint4*>(a.inputs[r] + off)[p] : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[8 * p + j] = __fadd_rn(acc[8 * p + j], t[j]);
+    for (int p = 0; p < 4; ++p) rres[p] = reinterpret_cast<const uint4*>(a.residual + off)[p];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) bf16x8_to_f32(raw[0][p], acc + 8 * p);
+#pragma unroll
+    for (int r = 1; r < kArMaxInputs; ++r) {
+      if (r < a.num_inputs) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          bf16x8_to_f32(raw[r][p], t);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[8 * p + j] = __fadd_rn(acc[8 * p + j], t[j]);
+        }
       }
     }
     uint32_t packed[16];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      bf16x8_to_f32(reinterpret_cast<const uint4*>(a.residual + off)[p], t);
+      bf16x8_to_f32(rres[p], t);
 #pragma unroll
       for (int j = 0; j < 8; ++j) c[8 * p + j] = round_bf16(__fadd_rn(acc[8 * p + j], t[j]));
     }
@@ -104,7 +117,7 @@ __global__ void __launch_bounds__(1024) ar_norm_quant_kernel(const __grid_consta
   float wt[8];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    bf16x8_to_f32(reinterpret_cast<const uint4*>(a.weight + 32 * g)[p], wt);
+    bf16x8_to_f32(wraw[p], wt);
 #pragma unroll
     for (int j = 0; j < 8; ++j) out[8 * p + j] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(c[8 * p + j], r)), wt[j]));
   }

@@ -597,7 +597,9 @@ def run_ar_norm(args, rank, world, local_rank):
         # the ranks' real partial buffers, read over NVLink
         peers = tp.PeerPartials(rows, hidden, dev)
         peers.local.copy_(torch.randn(rows, hidden, generator=g, device=dev).to(bf))
-        sets = [dict(inputs=peers.buffers, res=torch.randn(rows, hidden, generator=g, device=dev).to(bf))
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local_rank])  # every rank's partial is written before any rank reads it
+        sets = [dict(inputs=peers.ptrs, res=torch.randn(rows, hidden, generator=g, device=dev).to(bf))
                 for _ in range(AR_SETS)]
         ranks = world
     else:
@@ -661,7 +663,7 @@ def run_ar_norm(args, rank, world, local_rank):
         ms = timed(fused, graphed=True)
     ms_unfused = timed(unfused, graphed=True) if world == 1 else None
     if world > 1:
-        del sets, peers
+        peers.close()
     if rank != 0:
         return None
     peak, peak_kind = _peak_hbm()

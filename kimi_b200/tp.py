@@ -11,7 +11,8 @@ of it, reading the ranks' partials straight from their buffers.
 * :func:`ar_rmsnorm_mxfp4` runs the kernel on a list of partial buffers the
   current GPU can read (its own, and peers' mapped over NVLink).
 * :class:`PeerPartials` maps every rank's partial buffer into every rank
-  (CUDA IPC handles exchanged through ``torch.distributed``) and orders the
+  (CUDA IPC handles exchanged through ``torch.distributed``, each opened with
+  the reading GPU current, so that GPU's kernels may read it) and orders the
   kernel between two stream-ordered barriers: the partials are complete
   before any rank reads them, and no rank overwrites its partial until every
   rank has read it.  The kernel itself waits for nothing.
@@ -34,18 +35,26 @@ def ar_rmsnorm_mxfp4(inputs, residual: torch.Tensor, weight: torch.Tensor, eps: 
     * weight)``, and ``out`` quantised to MXFP4: returns ``(residual_out,
     nibbles uint8 [rows, hidden/2], scales uint8 [rows, hidden/32])``.
 
-    ``inputs``: 1..8 bf16 [rows, hidden] contiguous tensors (rank order) the
-    residual's GPU can read; ``residual`` bf16 [rows, hidden] contiguous,
+    ``inputs``: 1..8 partials in rank order, each a bf16 [rows, hidden]
+    contiguous CUDA tensor or the integer device address of one (a peer's
+    buffer mapped into this process, as :class:`PeerPartials` gives), readable
+    from the residual's GPU; ``residual`` bf16 [rows, hidden] contiguous,
     ``weight`` bf16 [hidden].  ``residual_out`` may be ``residual`` itself.
     """
     dev = _require_cuda(residual, weight)
-    inputs = list(inputs)
-    if not 1 <= len(inputs) <= _lib.AR_MAX_INPUTS:
-        raise ValueError(f"1..{_lib.AR_MAX_INPUTS} inputs")
+    if residual.dim() != 2 or residual.dtype != torch.bfloat16 or not residual.is_contiguous():
+        raise ValueError("residual must be a contiguous bf16 [rows, hidden] tensor")
     rows, hidden = residual.shape
-    for t in inputs + [residual]:
+    input_ptrs = []
+    for t in inputs:
+        if isinstance(t, int):
+            input_ptrs.append(t)
+            continue
         if t.dtype != torch.bfloat16 or t.shape != (rows, hidden) or not t.is_contiguous() or t.device.type != "cuda":
-            raise ValueError("inputs and residual must be contiguous bf16 CUDA tensors of one shape [rows, hidden]")
+            raise ValueError("inputs must be contiguous bf16 CUDA tensors of the residual's shape [rows, hidden]")
+        input_ptrs.append(t.data_ptr())
+    if not 1 <= len(input_ptrs) <= _lib.AR_MAX_INPUTS:
+        raise ValueError(f"1..{_lib.AR_MAX_INPUTS} inputs")
     if weight.dtype != torch.bfloat16 or weight.shape != (hidden,) or not weight.is_contiguous():
         raise ValueError("weight must be a contiguous bf16 [hidden] tensor")
     if residual_out is None:
@@ -55,9 +64,9 @@ def ar_rmsnorm_mxfp4(inputs, residual: torch.Tensor, weight: torch.Tensor, eps: 
     if scales is None:
         scales = torch.empty(rows, hidden // 32, dtype=torch.uint8, device=dev)
     p = _lib.KimiArRmsNormParams()
-    for i, t in enumerate(inputs):
-        p.inputs[i] = t.data_ptr()
-    p.num_inputs = len(inputs)
+    for i, ptr in enumerate(input_ptrs):
+        p.inputs[i] = int(ptr)
+    p.num_inputs = len(input_ptrs)
     p.residual, p.residual_out, p.weight = residual.data_ptr(), residual_out.data_ptr(), weight.data_ptr()
     p.eps = float(eps)
     p.nibbles, p.scales = nibbles.data_ptr(), scales.data_ptr()
@@ -68,32 +77,67 @@ def ar_rmsnorm_mxfp4(inputs, residual: torch.Tensor, weight: torch.Tensor, eps: 
     return residual_out, nibbles, scales
 
 
+def _check_cuda(err, what):
+    if int(err) != 0:
+        raise RuntimeError(f"{what} failed: CUDA error {int(err)}")
+
+
 class PeerPartials:
     """One partial buffer bf16 [rows, hidden] per rank, mapped into every rank.
 
     Collective constructor (every rank of ``group`` calls it with the same
     shape): each rank allocates its buffer, and the buffers' CUDA IPC handles
     are exchanged with ``all_gather_object``.  ``local`` is this rank's buffer
-    (the o_proj output is written there); :meth:`reduce_norm_quant` runs the
-    fused kernel over all ranks' buffers between two barriers.
+    (the o_proj output is written there); ``ptrs`` are every rank's buffer as
+    device addresses this rank's GPU reads (rank order);
+    :meth:`reduce_norm_quant` runs the fused kernel over them between two
+    barriers; :meth:`close` (collective) unmaps the peers' buffers.
     """
 
     def __init__(self, rows: int, hidden: int, device: torch.device, group=None):
         import torch.distributed as dist
-        from torch.multiprocessing.reductions import reduce_tensor
+        from cuda.bindings import driver, runtime
 
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         if self.world > _lib.AR_MAX_INPUTS:
             raise ValueError(f"at most {_lib.AR_MAX_INPUTS} ranks")
-        self.local = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=device)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, reduce_tensor(self.local), group=group)
-        self.buffers = []
-        for r, (fn, args) in enumerate(handles):
-            self.buffers.append(self.local if r == self.rank else fn(*args))
-        self.device = device
+        self.device = torch.device(device)
+        self.local = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=self.device)
+        ptr = self.local.data_ptr()
+        # the IPC handle names the whole allocation the tensor lies in
+        err, base, _ = driver.cuMemGetAddressRange(driver.CUdeviceptr(ptr))
+        _check_cuda(err, "cuMemGetAddressRange")
+        err, handle = runtime.cudaIpcGetMemHandle(int(base))
+        _check_cuda(err, "cudaIpcGetMemHandle")
+        shared = [None] * self.world
+        dist.all_gather_object(shared, (bytes(handle.reserved), ptr - int(base)), group=group)
+        # open every peer's allocation with this rank's GPU current: the mapping
+        # (and the peer access it enables) belongs to this GPU's context
+        err, = runtime.cudaSetDevice(self.device.index)
+        _check_cuda(err, "cudaSetDevice")
+        self._opened, self.ptrs = [], []
+        for r, (raw, offset) in enumerate(shared):
+            if r == self.rank:
+                self.ptrs.append(ptr)
+                continue
+            h = runtime.cudaIpcMemHandle_t()
+            h.reserved = raw
+            err, peer_base = runtime.cudaIpcOpenMemHandle(h, runtime.cudaIpcMemLazyEnablePeerAccess)
+            _check_cuda(err, "cudaIpcOpenMemHandle")
+            self._opened.append(peer_base)
+            self.ptrs.append(int(peer_base) + offset)
+
+    def close(self):
+        """Unmap the peers' buffers (collective: call on every rank once no
+        kernel reads them any more)."""
+        from cuda.bindings import runtime
+        torch.cuda.synchronize(self.device)
+        for b in self._opened:
+            runtime.cudaIpcCloseMemHandle(b)
+        self._opened, self.ptrs = [], []
+        self._barrier()
 
     def _barrier(self):
         import torch.distributed as dist
@@ -106,7 +150,6 @@ class PeerPartials:
         """All-reduce of the ranks' ``local`` buffers + residual + RMSNorm +
         MXFP4 (every rank computes the full result for its own use)."""
         self._barrier()  # every rank's partial is written
-        out = ar_rmsnorm_mxfp4(self.buffers, residual, weight, eps, residual_out=residual_out,
-                               legacy_rule=legacy_rule)
+        out = ar_rmsnorm_mxfp4(self.ptrs, residual, weight, eps, residual_out=residual_out, legacy_rule=legacy_rule)
         self._barrier()  # every rank has read every partial
         return out

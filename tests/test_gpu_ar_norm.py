@@ -83,7 +83,7 @@ def _two_rank_worker(rank, world, port, result_dir):
               and np.array_equal(sc.cpu().numpy(), sc_ref))
         with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
             f.write("ok" if ok else "mismatch")
-        del peers
+        peers.close()
     finally:
         dist.destroy_process_group()
 

@@ -668,7 +668,10 @@ def run_ar_norm(args, rank, world, local_rank):
         return None
     peak, peak_kind = _peak_hbm()
     nbytes = rows * hidden * 2 * (ranks + 2) + rows * hidden // 2 + rows * hidden // 32 + hidden * 2
-    achieved = nbytes / (ms * 1e-3) / 1e9
+    # with peers the bound is the bytes that cross NVLink into this GPU (the
+    # other ranks' partials) at the measured 770 GB/s peer-copy rate per direction
+    link_bytes = rows * hidden * 2 * (ranks - 1)
+    achieved = (nbytes if world == 1 else link_bytes) / (ms * 1e-3) / 1e9
     line = {
         "metric": "TP8 layer-input step (all-reduce of 8 partials + residual + RMSNorm + MXFP4), Kimi-K2 hidden 7168",
         "value": round(ms * 1e3, 3), "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -682,9 +685,11 @@ def run_ar_norm(args, rank, world, local_rank):
                    "timing": "CUDA graph of the kernel calls replayed; device time per call"},
         "gpu_launches": max(1, args.steps // AR_SETS) * AR_SETS,
         "roofline": {"bound": "hbm" if world == 1 else "nvlink", "achieved": round(achieved, 1),
-                     "peak": peak if world == 1 else 770.0 * (ranks - 1) / ranks * ranks,
+                     "peak": peak if world == 1 else 770.0,
                      "unit": "GB/s", "frac": None, "traffic": None,
-                     "note": f"{nbytes} algorithmic bytes per call"},
+                     "note": f"{nbytes} algorithmic bytes per call" if world == 1 else
+                             f"{link_bytes} bytes over NVLink into this GPU per call ({nbytes} in all); "
+                             "peak = measured peer copy per direction"},
         "clocks": clocks.summary(),
     }
     line["roofline"]["frac"] = round(achieved / line["roofline"]["peak"], 4)

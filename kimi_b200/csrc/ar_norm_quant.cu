@@ -16,8 +16,12 @@
 // MXFP4 group -- so the only cross-thread step is the sum of squares: the
 // thread's 32 squares in order, a warp butterfly (lane 0's value kept), the
 // warps in order.  Every float32 step is the oracle's, so the results are
-// bit-exact.  Loads and stores are 16-byte vectors; the kernel is one pass
-// over the inputs (bound by HBM or, for peer inputs, by NVLink).
+// bit-exact.  The kernel is one pass over the inputs (bound by HBM or, for
+// peer inputs, by NVLink).  A warp reads its 32 groups (2 KB of each input) as
+// four fully coalesced 16-byte loads per lane, so every 32-byte sector is
+// requested once (which matters for peer reads, where nothing merges partial
+// requests), then hands each lane its own group's 64 bytes through a swizzled
+// 2 KB shared-memory stage.
 //
 // The caller orders the kernel after every rank's partial is complete and
 // keeps each partial unchanged until every rank's kernel has read it (for
@@ -42,32 +46,68 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float* x) {
 
 __device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// The warp's 128 uint4 of one input, loaded coalesced (lane l holds slots
+// 32 p + l), are handed back as lane l's own group (slots 4 l .. 4 l + 3).
+// Slot s lives at s ^ ((s >> 3) & 3): both the stores (8 consecutive slots per
+// quarter warp) and the loads (stride 4 slots) then hit 8 distinct 16-byte
+// bank groups per quarter warp.
+__device__ __forceinline__ void warp_regroup(uint4 (&v)[4], uint4* stage, int lane) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int s = 32 * p + lane;
+    stage[s ^ ((s >> 3) & 3)] = v[p];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int s = 4 * lane + p;
+    v[p] = stage[s ^ ((s >> 3) & 3)];
+  }
+  __syncwarp();
+}
+
 template <bool LEGACY>
 __global__ void __launch_bounds__(256) ar_norm_quant_kernel(const __grid_constant__ ArNormArgs a) {
   __shared__ float warp_sum[32];
   __shared__ float rstd;
+  __shared__ uint4 stage[8][128];  // one 2 KB regroup stage per warp (at most 256 threads)
   const int row = blockIdx.x, g = threadIdx.x, lane = g & 31, warp = g >> 5;
   const int groups = a.hidden / 32;
   const bool live = g < groups;
   const int64_t off = static_cast<int64_t>(row) * a.hidden + 32 * g;
+  // the warp's span: groups 32 warp .. 32 warp + warp_groups - 1 (every warp
+  // has at least one, the launch rounds the groups up to whole warps)
+  const int warp_groups = min(32, groups - 32 * warp);
+  const int64_t span = (static_cast<int64_t>(row) * a.hidden + 1024 * warp) / 8;  // in uint4
+
+  // every rank's slots and the residual's are loaded first (all in flight
+  // together), then regrouped, summed in rank order, the residual added
+  uint4 raw[kArMaxInputs][4], rres[4], wraw[4];
+#pragma unroll
+  for (int r = 0; r < kArMaxInputs; ++r)
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+      raw[r][p] = r < a.num_inputs && 32 * p + lane < 4 * warp_groups
+                      ? reinterpret_cast<const uint4*>(a.inputs[r])[span + 32 * p + lane]
+                      : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+  for (int p = 0; p < 4; ++p)
+    rres[p] = 32 * p + lane < 4 * warp_groups ? reinterpret_cast<const uint4*>(a.residual)[span + 32 * p + lane]
+                                              : make_uint4(0u, 0u, 0u, 0u);
+  if (live) {  // the weight is read by every row: left to the caches, 64 bytes per lane
+#pragma unroll
+    for (int p = 0; p < 4; ++p) wraw[p] = reinterpret_cast<const uint4*>(a.weight + 32 * g)[p];
+  }
+  uint4* st = stage[warp];
+#pragma unroll
+  for (int r = 0; r < kArMaxInputs; ++r)
+    if (r < a.num_inputs) warp_regroup(raw[r], st, lane);  // uniform over the block
+  warp_regroup(rres, st, lane);
 
   float c[32];
   float sq = 0.f;
-  uint4 wraw[4];  // the weight's 64 bytes, loaded with the partials
   if (live) {
-#pragma unroll
-    for (int p = 0; p < 4; ++p) wraw[p] = reinterpret_cast<const uint4*>(a.weight + 32 * g)[p];
     float acc[32], t[8];
-    // every rank's 64 bytes and the residual's are loaded first (all in
-    // flight together), then summed in rank order, then the residual added
-    uint4 raw[kArMaxInputs][4], rres[4];
-#pragma unroll
-    for (int r = 0; r < kArMaxInputs; ++r)
-#pragma unroll
-      for (int p = 0; p < 4; ++p)
-        raw[r][p] = r < a.num_inputs ? reinterpret_cast<const uint4*>(a.inputs[r] + off)[p] : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int p = 0; p < 4; ++p) rres[p] = reinterpret_cast<const uint4*>(a.residual + off)[p];
 #pragma unroll
     for (int p = 0; p < 4; ++p) bf16x8_to_f32(raw[0][p], acc + 8 * p);
 #pragma unroll

@@ -104,6 +104,7 @@ class PeerPartials:
         if self.world > _lib.AR_MAX_INPUTS:
             raise ValueError(f"at most {_lib.AR_MAX_INPUTS} ranks")
         self.device = torch.device(device)
+        self.rows, self.hidden = rows, hidden
         self.local = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=self.device)
         ptr = self.local.data_ptr()
         # the IPC handle names the whole allocation the tensor lies in
@@ -148,7 +149,12 @@ class PeerPartials:
     def reduce_norm_quant(self, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
                           residual_out: torch.Tensor | None = None, legacy_rule: bool = False):
         """All-reduce of the ranks' ``local`` buffers + residual + RMSNorm +
-        MXFP4 (every rank computes the full result for its own use)."""
+        MXFP4 (every rank computes the full result for its own use) over the
+        first ``residual.shape[0]`` rows of every rank's buffer."""
+        if residual.dim() != 2 or residual.shape[0] > self.rows or residual.shape[1] != self.hidden:
+            raise ValueError(f"residual must be [<= {self.rows}, {self.hidden}]")
+        if not self.ptrs:
+            raise RuntimeError("PeerPartials is closed")
         self._barrier()  # every rank's partial is written
         out = ar_rmsnorm_mxfp4(self.ptrs, residual, weight, eps, residual_out=residual_out, legacy_rule=legacy_rule)
         self._barrier()  # every rank has read every partial

@@ -35,7 +35,8 @@ def _bits(t):
 
 
 @pytest.mark.parametrize("n,rows,hidden,legacy", [(1, 1, 7168, False), (2, 128, 7168, False),
-                                                  (8, 64, 7168, False), (4, 3, 2080, True)])
+                                                  (8, 64, 7168, False), (4, 3, 2080, True),
+                                                  (3, 5, 8192, False), (2, 2, 32, True)])
 def test_matches_oracle(n, rows, hidden, legacy):
     rng = np.random.default_rng(60 + n + rows)
     ins = [_bf16_np(rng, (rows, hidden), 0.5) for _ in range(n)]

@@ -9,7 +9,7 @@ library's KV-append quantiser).  A step is one decode call over the whole
 batch (one layer).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload kimi_k2|ragged|tp8_prologue|tp8_ar_norm]
+                    [--workload kimi_k2|ragged|tp8_prologue|tp8_ar_norm|tp8_vup_oproj]
 
 ``--workload ragged`` runs the batch-sharded sweep instead: one batch of 256
 sequences with lengths drawn uniformly from 1K-32K tokens (seeded), spread
@@ -25,6 +25,10 @@ call, next to the same step as separate torch / library calls.
 all-reduce (kimi_b200.tp: 8 partials + residual + RMSNorm + MXFP4): on one GPU
 with 8 local buffers standing in for the ranks, under torchrun with every
 rank's real buffer read over NVLink.
+``--workload tp8_vup_oproj`` times the decode step after attention: the V
+up-projection of the heads-first output by W_UV, then o_proj
+(kimi_b200.v_up_proj_and_o_proj) at the Kimi-K2 TP8 shape per GPU (8 heads,
+128 tokens, hidden 7168), next to the reference's torch.bmm + torch.mm path.
 
 Prints one JSON line on rank 0.  ``value`` is the aggregate achieved HBM
 bandwidth over all ranks computed from the algorithmic bytes (latent nibbles
@@ -699,13 +703,109 @@ def run_ar_norm(args, rank, world, local_rank):
     return line
 
 
+# ---------------------------------------------------------------------------
+# the decode step after attention at the Kimi-K2 TP8 shape per GPU: W_UV BMM of
+# the heads-first output, then o_proj [1024 -> 7168]
+# ---------------------------------------------------------------------------
+VU_TOKENS, VU_HEADS, VU_HIDDEN, VU_SETS = 128, 8, 7168, 8
+
+
+def run_vup(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import kimi_b200 as kimi
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T, H, D = VU_TOKENS, VU_HEADS, VU_HIDDEN
+    g = torch.Generator(device=dev).manual_seed(17 + 1000 * rank)
+    bf = torch.bfloat16
+    # VU_SETS independent layers' inputs and weights (~148 MB, more than the 126 MB L2), used in turn
+    sets = [dict(o=torch.randn(16, T, 512, generator=g, device=dev).to(bf)[:H],  # heads-first, 16 padded heads
+                 w_uv=(torch.randn(H, 512, 128, generator=g, device=dev) * 0.02).to(bf),
+                 w_o=(torch.randn(D, H * 128, generator=g, device=dev) * 0.02).to(bf),
+                 x=torch.empty(T, H * 128, dtype=bf, device=dev),
+                 out=torch.empty(T, D, dtype=bf, device=dev)) for _ in range(VU_SETS)]
+
+    def fused(i):
+        s_ = sets[i % VU_SETS]
+        kimi.v_up_proj_and_o_proj(s_["o"], s_["w_uv"], s_["w_o"], out=s_["out"], x=s_["x"])
+
+    def unfused(i):  # the reference's path: fp32 BMM, bf16 round, transpose, bf16 mm (cuBLAS)
+        s_ = sets[i % VU_SETS]
+        x = torch.bmm(s_["o"].float(), s_["w_uv"].float()).to(bf).transpose(0, 1).reshape(T, H * 128)
+        torch.mm(x, s_["w_o"].T, out=s_["out"])
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(VU_SETS):
+                fn(i)
+        reps = max(1, args.steps // VU_SETS)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * VU_SETS)
+        del graph
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with ClockSampler(dev.index) as clocks:
+        ms = timed(fused)
+    ms_unfused = timed(unfused)
+    if rank != 0:
+        return None
+    peak, peak_kind = _peak_hbm()
+    # o + W_UV + W_o read, out written (the x scratch round trip stays in L2)
+    nbytes = (H * T * 512 + H * 512 * 128 + D * H * 128 + T * D) * 2
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    flops = 2 * T * (H * 512 * 128 + H * 128 * D)
+    return {
+        "metric": "decode epilogue latency (V up-projection by W_UV + o_proj), Kimi-K2 TP8 per GPU",
+        "value": round(ms * 1e3, 3), "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 6), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded normal heads-first o, W_UV and W_o ~ N(0, 0.02))",
+        "config": {"workload": f"Kimi-K2 TP8 decode epilogue: {H} heads per GPU sliced from 16 padded, {T} tokens, "
+                               f"W_UV [{H}, 512, 128], o_proj [{H * 128} -> {D}]",
+                   "l2": f"inputs larger than L2: {VU_SETS} independent layers' inputs and weights used in turn",
+                   "parallelism": f"{world} replica(s), one per GPU, no collective"},
+        "gpu_launches": max(1, args.steps // VU_SETS) * VU_SETS * 2,
+        "timing": f"CUDA graph of {VU_SETS} calls (two launches each) replayed; device time per call",
+        "unfused_us": round(ms_unfused * 1e3, 3),
+        "unfused_path": "torch.bmm (fp32) + bf16 round + transpose + torch.mm (the reference's path)",
+        "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "note": f"{nbytes} algorithmic bytes per call ({flops} FLOPs: far below the tensor roofline)"},
+        "clocks": clocks.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "tp8_prologue", "tp8_ar_norm"], default="kimi_k2")
+    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "tp8_prologue", "tp8_ar_norm", "tp8_vup_oproj"],
+                    default="kimi_k2")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
                     help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
     args = ap.parse_args()
@@ -729,7 +829,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        runner = {"tp8_prologue": run_prologue, "tp8_ar_norm": run_ar_norm}.get(args.workload, run_ours)
+        runner = {"tp8_prologue": run_prologue, "tp8_ar_norm": run_ar_norm,
+                  "tp8_vup_oproj": run_vup}.get(args.workload, run_ours)
         line = runner(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)

@@ -270,6 +270,35 @@ typedef struct KimiArRmsNormParams {
 
 KIMI_API int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* params, void* stream);
 
+/* The decode step after attention: V up-projection of the heads-first latent
+ * output, then o_proj.  Replaces `MLAAttention._v_up_proj_and_o_proj(o,
+ * heads_first=True)` (patches/atom-optimizations.patch:131-143, called at
+ * :297-302 on the decode's heads-first output; tests/test_mla_heads_first_e2e.py:50-59):
+ *   x[t, h * 128 + v] = bf16(sum_l o[h, t, l] * w_uv[h, l, v])   (fp32 accumulation)
+ *   out[t, :]         = bf16(x[t, :] @ w_o^T)                      (fp32 accumulation)
+ * o: bf16 [num_heads, num_tokens, 512] with element strides o_stride_h /
+ * o_stride_t (latent dimension contiguous), w_uv bf16 [num_heads, 512, 128]
+ * contiguous, w_o bf16 [hidden, num_heads * 128] contiguous (the o_proj
+ * Linear weight), x a bf16 [num_tokens, num_heads * 128] contiguous scratch
+ * (the BMM result, also readable afterwards), out bf16 [num_tokens, hidden]
+ * with row stride out_stride.  num_heads 1..8, hidden a multiple of 64.
+ * Two launches on `stream`, the second a programmatic dependent of the first. */
+typedef struct KimiVUpOProjParams {
+  const void* o;
+  int64_t o_stride_h;
+  int64_t o_stride_t;
+  const void* w_uv;
+  const void* w_o;
+  void* x;
+  void* out;
+  int64_t out_stride;
+  int32_t num_tokens;
+  int32_t num_heads;
+  int32_t hidden;
+} KimiVUpOProjParams;
+
+KIMI_API int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* params, void* stream);
+
 /* Row quantiser: x bf16 [rows, cols] (row stride x_stride elements, cols a
  * multiple of 32) -> nibbles uint8 [rows, cols/2] and scales uint8
  * [rows, cols/32], both contiguous. */

@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "kimi_mla_decode_merge",
     "kimi_mla_q_absorb_rope_append",
     "kimi_ar_rmsnorm_mxfp4",
+    "kimi_mla_v_up_o_proj",
 )
 
 AR_MAX_INPUTS = 8
@@ -132,6 +133,22 @@ class KimiArRmsNormParams(ctypes.Structure):
     ]
 
 
+class KimiVUpOProjParams(ctypes.Structure):
+    _fields_ = [
+        ("o", ctypes.c_void_p),
+        ("o_stride_h", ctypes.c_int64),
+        ("o_stride_t", ctypes.c_int64),
+        ("w_uv", ctypes.c_void_p),
+        ("w_o", ctypes.c_void_p),
+        ("x", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_stride", ctypes.c_int64),
+        ("num_tokens", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -174,6 +191,8 @@ def load() -> ctypes.CDLL:
         lib.kimi_mla_q_absorb_rope_append.argtypes = [ctypes.POINTER(KimiQAbsorbParams), vp]
         lib.kimi_ar_rmsnorm_mxfp4.restype = ctypes.c_int
         lib.kimi_ar_rmsnorm_mxfp4.argtypes = [ctypes.POINTER(KimiArRmsNormParams), vp]
+        lib.kimi_mla_v_up_o_proj.restype = ctypes.c_int
+        lib.kimi_mla_v_up_o_proj.argtypes = [ctypes.POINTER(KimiVUpOProjParams), vp]
         lib.kimi_mxfp4_quantize.restype = ctypes.c_int
         lib.kimi_mxfp4_quantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, vp]
         _lib = lib

@@ -461,6 +461,33 @@ int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* p, void* stream) {
   return cuda_status(kimi::launch_ar_norm_quant(a, static_cast<cudaStream_t>(stream)));
 }
 
+int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* p, void* stream) {
+  if (!p) return KIMI_ERR_NULL_POINTER;
+  if (p->num_tokens < 0 || p->num_heads < 1 || p->num_heads > 8 || p->hidden < 64 || p->hidden % 64)
+    return KIMI_ERR_BAD_SHAPE;
+  if (p->num_tokens == 0) return KIMI_OK;
+  if (!p->o || !p->w_uv || !p->w_o || !p->x || !p->out) return KIMI_ERR_NULL_POINTER;
+  if (p->o_stride_t % 8 || p->o_stride_h % 8 || p->o_stride_t < 512 || p->o_stride_h < 0 || p->out_stride % 8 ||
+      p->out_stride < p->hidden)
+    return KIMI_ERR_BAD_STRIDE;
+  if (!aligned(p->o, 16) || !aligned(p->w_uv, 16) || !aligned(p->w_o, 16) || !aligned(p->x, 16) ||
+      !aligned(p->out, 16))
+    return KIMI_ERR_MISALIGNED;
+  kimi::VUpOProjArgs a;
+  a.o = static_cast<const __nv_bfloat16*>(p->o);
+  a.o_stride_h = p->o_stride_h;
+  a.o_stride_t = p->o_stride_t;
+  a.w_uv = static_cast<const __nv_bfloat16*>(p->w_uv);
+  a.w_o = static_cast<const __nv_bfloat16*>(p->w_o);
+  a.x = static_cast<__nv_bfloat16*>(p->x);
+  a.out = static_cast<__nv_bfloat16*>(p->out);
+  a.out_stride = p->out_stride;
+  a.num_tokens = p->num_tokens;
+  a.num_heads = p->num_heads;
+  a.hidden = p->hidden;
+  return cuda_status(kimi::launch_v_up_o_proj(a, static_cast<cudaStream_t>(stream)));
+}
+
 int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,
                         int32_t legacy_rule, void* stream) {
   if (rows < 0 || cols < 0 || cols % 32) return KIMI_ERR_BAD_SHAPE;

@@ -85,6 +85,20 @@ struct ArNormArgs {
   int legacy_rule;
 };
 
+struct VUpOProjArgs {
+  const __nv_bfloat16* o;  // [num_heads, num_tokens, 512], element strides below
+  int64_t o_stride_h;
+  int64_t o_stride_t;
+  const __nv_bfloat16* w_uv;  // [num_heads, 512, 128]
+  const __nv_bfloat16* w_o;   // [hidden, num_heads * 128]
+  __nv_bfloat16* x;           // [num_tokens, num_heads * 128] scratch
+  __nv_bfloat16* out;         // [num_tokens, hidden], row stride out_stride
+  int64_t out_stride;
+  int num_tokens;
+  int num_heads;
+  int hidden;
+};
+
 struct QuantizeArgs {
   const __nv_bfloat16* x;
   int64_t rows;
@@ -158,6 +172,7 @@ struct ReduceArgs {
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);
 cudaError_t launch_q_absorb(const QAbsorbArgs& a, cudaStream_t stream);
 cudaError_t launch_ar_norm_quant(const ArNormArgs& a, cudaStream_t stream);
+cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream);

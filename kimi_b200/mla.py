@@ -314,6 +314,53 @@ def q_absorb_rope_append(q_nope: torch.Tensor, q_pe: torch.Tensor, w_uk: torch.T
     return q_out
 
 
+def v_up_proj_and_o_proj(o: torch.Tensor, w_uv: torch.Tensor, w_o: torch.Tensor, out: torch.Tensor | None = None,
+                         x: torch.Tensor | None = None) -> torch.Tensor:
+    """The decode step after attention (the reference's
+    ``_v_up_proj_and_o_proj(o, heads_first=True)``,
+    patches/atom-optimizations.patch:131-143 and :297-302):
+
+    * ``x[t, h*128:(h+1)*128] = bf16(o[h, t] @ w_uv[h])`` (fp32 accumulation);
+    * ``out[t] = bf16(x[t] @ w_o.T)`` (fp32 accumulation).
+
+    ``o`` is the decode's heads-first output bf16 [H, T, 512] (a slice of the
+    padded heads, latent dim contiguous), ``w_uv`` bf16 [H, 512, 128] and
+    ``w_o`` bf16 [hidden, H * 128] contiguous (H <= 8, hidden % 64 == 0).
+    ``out`` (bf16 [T, hidden], last dim contiguous, allocated when None) is
+    returned: this rank's partial of the tensor-parallel all-reduce, so it
+    may be a :class:`kimi_b200.tp.PeerPartials` ``local`` buffer.  ``x`` is a
+    bf16 [T, H * 128] contiguous scratch (allocated when None) that holds the
+    up-projection afterwards.
+    """
+    dev = _require_cuda(o, w_uv, w_o)
+    for name, t in (("o", o), ("w_uv", w_uv), ("w_o", w_o)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bfloat16")
+    if o.dim() != 3 or o.shape[2] != KV_LORA_RANK or o.stride(2) != 1:
+        raise ValueError("o must be heads-first [H, T, 512] with a contiguous last dim")
+    H, T = o.shape[0], o.shape[1]
+    if w_uv.shape != (H, KV_LORA_RANK, 128) or not w_uv.is_contiguous():
+        raise ValueError("w_uv must be a contiguous [H, 512, 128] tensor")
+    if w_o.dim() != 2 or w_o.shape[1] != H * 128 or not w_o.is_contiguous():
+        raise ValueError("w_o must be a contiguous [hidden, H * 128] tensor")
+    hidden = w_o.shape[0]
+    if out is None:
+        out = torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
+    if out.dtype != torch.bfloat16 or out.dim() != 2 or out.shape != (T, hidden) or out.stride(1) != 1:
+        raise ValueError("out must be a bf16 [T, hidden] tensor with a contiguous last dim")
+    if x is None:
+        x = torch.empty(T, H * 128, dtype=torch.bfloat16, device=dev)
+    if x.dtype != torch.bfloat16 or x.shape != (T, H * 128) or not x.is_contiguous():
+        raise ValueError("x must be a contiguous bf16 [T, H * 128] tensor")
+    p = _lib.KimiVUpOProjParams(o=o.data_ptr(), o_stride_h=o.stride(0), o_stride_t=o.stride(1), w_uv=w_uv.data_ptr(),
+                                w_o=w_o.data_ptr(), x=x.data_ptr(), out=out.data_ptr(), out_stride=out.stride(0),
+                                num_tokens=T, num_heads=H, hidden=hidden)
+    with torch.cuda.device(dev):
+        status = _lib.load().kimi_mla_v_up_o_proj(ctypes.byref(p), _stream_handle(dev))
+    _lib.check(status, "kimi_mla_v_up_o_proj")
+    return out
+
+
 def mxfp4_quantize(x: torch.Tensor, legacy_rule: bool = False):
     """bf16 [rows, cols] (cols % 32 == 0) -> (nibbles u8 [rows, cols/2], scales u8 [rows, cols/32])."""
     dev = _require_cuda(x)

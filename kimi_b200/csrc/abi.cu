@@ -120,6 +120,18 @@ bool encode_cache_maps(const void* kv_buffer, const void* kv_scales, int64_t num
   return true;
 }
 
+// A bf16 tensor map with 128-byte swizzle over `rank` dimensions (innermost
+// first; strides in bytes for dimensions 1 ..), boxes of 64 elements (128 B)
+// innermost.  Reads outside the tensor yield zeros.
+bool encode_bf16_map(CUtensorMap& m, const void* base, cuuint32_t rank, const cuuint64_t* dims,
+                     const cuuint64_t* strides, const cuuint32_t* box) {
+  const EncodeTiledFn enc = encode_tiled();
+  const cuuint32_t unit[3] = {1, 1, 1};
+  return enc && enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, unit,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // How one call is laid out on the GPU.
 //  * requested splits S > 0: split mode, every sequence cut into S equal tile
 //    ranges (the reference's num_kv_splits), S = 1 writing the output directly;
@@ -467,8 +479,8 @@ int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* p, void* stream) {
     return KIMI_ERR_BAD_SHAPE;
   if (p->num_tokens == 0) return KIMI_OK;
   if (!p->o || !p->w_uv || !p->w_o || !p->x || !p->out) return KIMI_ERR_NULL_POINTER;
-  if (p->o_stride_t % 8 || p->o_stride_h % 8 || p->o_stride_t < 512 || p->o_stride_h < 0 || p->out_stride % 8 ||
-      p->out_stride < p->hidden)
+  if (p->o_stride_t % 8 || p->o_stride_h % 8 || p->o_stride_t < 512 || p->o_stride_h < 0 ||
+      (p->num_heads > 1 && p->o_stride_h == 0) || p->out_stride % 8 || p->out_stride < p->hidden)
     return KIMI_ERR_BAD_STRIDE;
   if (!aligned(p->o, 16) || !aligned(p->w_uv, 16) || !aligned(p->w_o, 16) || !aligned(p->x, 16) ||
       !aligned(p->out, 16))
@@ -485,7 +497,32 @@ int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* p, void* stream) {
   a.num_tokens = p->num_tokens;
   a.num_heads = p->num_heads;
   a.hidden = p->hidden;
-  return cuda_status(kimi::launch_v_up_o_proj(a, static_cast<cudaStream_t>(stream)));
+  const cuuint64_t T = static_cast<cuuint64_t>(p->num_tokens), H = static_cast<cuuint64_t>(p->num_heads);
+  const cuuint64_t K = 128 * H, stride_t = 2 * static_cast<cuuint64_t>(p->o_stride_t);
+  // a single head's stride is never used: give it the extent of the tokens
+  const cuuint64_t stride_h = p->num_heads > 1 ? 2 * static_cast<cuuint64_t>(p->o_stride_h) : T * stride_t;
+  kimi::VUpOProjMaps maps;
+  {
+    const cuuint64_t dims[3] = {512, T, H}, strides[2] = {stride_t, stride_h};
+    const cuuint32_t box[3] = {64, 128, 1};
+    if (!encode_bf16_map(maps.o, p->o, 3, dims, strides, box)) return KIMI_ERR_BAD_STRIDE;
+  }
+  {
+    const cuuint64_t dims[2] = {128, 512 * H}, strides[1] = {256};
+    const cuuint32_t box[2] = {64, 64};
+    if (!encode_bf16_map(maps.w_uv, p->w_uv, 2, dims, strides, box)) return KIMI_ERR_UNSUPPORTED;
+  }
+  {
+    const cuuint64_t dims[2] = {K, T}, strides[1] = {2 * K};
+    const cuuint32_t box[2] = {64, 128};
+    if (!encode_bf16_map(maps.x, p->x, 2, dims, strides, box)) return KIMI_ERR_UNSUPPORTED;
+  }
+  {
+    const cuuint64_t dims[2] = {K, static_cast<cuuint64_t>(p->hidden)}, strides[1] = {2 * K};
+    const cuuint32_t box[2] = {64, 64};
+    if (!encode_bf16_map(maps.w_o, p->w_o, 2, dims, strides, box)) return KIMI_ERR_UNSUPPORTED;
+  }
+  return cuda_status(kimi::launch_v_up_o_proj(a, maps, static_cast<cudaStream_t>(stream)));
 }
 
 int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,

@@ -99,6 +99,17 @@ struct VUpOProjArgs {
   int hidden;
 };
 
+// TMA maps of the V up-projection + o_proj operands, all bf16 with 128-byte
+// swizzle: o as [H][T][512] (box 64 x 128 tokens x 1 head), W_UV as
+// [H * 512][128] (box 64 x 64 rows), x as [T][H * 128] (box 64 x 128 tokens),
+// W_o as [hidden][H * 128] (box 64 x 64 rows).
+struct VUpOProjMaps {
+  CUtensorMap o;
+  CUtensorMap w_uv;
+  CUtensorMap x;
+  CUtensorMap w_o;
+};
+
 struct QuantizeArgs {
   const __nv_bfloat16* x;
   int64_t rows;
@@ -172,7 +183,7 @@ struct ReduceArgs {
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);
 cudaError_t launch_q_absorb(const QAbsorbArgs& a, cudaStream_t stream);
 cudaError_t launch_ar_norm_quant(const ArNormArgs& a, cudaStream_t stream);
-cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, cudaStream_t stream);
+cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, const VUpOProjMaps& maps, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t stream);

@@ -243,6 +243,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tensor_map, i
       : "memory");
 }
 
+// 3-D tiled load of one box at element coordinates (x, y, z); otherwise as
+// tma_load_2d.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tensor_map, int x, int y, int z, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];\n" ::"r"(smem_addr(dst)),
+      "l"(tensor_map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(mbar))
+      : "memory");
+}
+
 // Untiled bulk copy global -> shared of `bytes` (a multiple of 16; both
 // addresses 16-byte aligned); the bytes count towards the mbarrier's
 // transaction count.

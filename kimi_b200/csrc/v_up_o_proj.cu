@@ -11,21 +11,25 @@
 // [H, 512, 128], W_o bf16 [hidden, H * 128] (the Linear weight), out bf16
 // [T, hidden] (this rank's partial of the tensor-parallel all-reduce).
 //
-// Two launches on one stream, the second a programmatic dependent of the first:
-//   * phase 1, one CTA per (head, 128-token tile, 64-column half of V): o's
-//     tile (A, K-major) and W_UV's half (B, MN-major as stored) copied with
-//     cp.async into 128-byte-swizzled shared memory (192 KB), 32 tcgen05.mma
-//     kind::f16 (M = 128 tokens, N = 64, K = 16) into TMEM, x written as bf16
+// Two launches on one stream, the second a programmatic dependent of the
+// first.  Every operand arrives by TMA (tiled, 128-byte swizzle: the UMMA
+// operand layout; no multicast) on mbarriers:
+//   * phase 1, one CTA per (head, 128-token tile, 64-column half of V): the 8
+//     K blocks of o's tile (A, K-major, 16 KB each) and of W_UV's half (B,
+//     MN-major as stored, 8 KB each) are all requested at once, one mbarrier
+//     per K block, and the MMAs of a block (tcgen05.mma kind::f16, M = 128
+//     tokens, N = 64, K = 16) issue as soon as it lands; x is written as bf16
 //     to a scratch [T, H * 128] that stays in L2;
-//   * phase 2, one CTA per 64 outputs of the hidden dimension: its whole W_o
-//     slice (64 x H * 128, at most 128 KB) is copied into shared memory BEFORE
-//     waiting for phase 1 (griddepcontrol.wait), so the weight stream -- the
-//     step's HBM traffic -- overlaps phase 1; then x streams through two
-//     32 KB stages (K = 128 each) and one thread issues the MMAs (M = 128
-//     tokens, N = 64); the CTA loops over 128-token tiles with its weights
-//     resident.
-// Every wait on an MMA commit is bounded; a give-up leaves that tile of the
-// output unwritten.
+//   * phase 2, one CTA per 64 outputs of the hidden dimension, warp roles:
+//     warp 0 lane 0 loads the CTA's whole W_o slice (64 x H * 128, at most
+//     128 KB, resident) BEFORE waiting for phase 1 (griddepcontrol.wait), so
+//     the weight stream -- the step's HBM traffic -- overlaps phase 1, then
+//     streams x through a ring of six 16 KB stages (K = 64 each); warp 1
+//     lane 0 issues the MMAs (M = 128 tokens, N = 64) into one of two TMEM
+//     accumulators; warps 4-7 read a finished accumulator and write out while
+//     the next token tile accumulates in the other.
+// Every wait is bounded; a give-up raises a shared abort flag that ends the
+// other roles' waits, and leaves the output unwritten or partly written.
 #include <cuda_runtime.h>
 
 #include "kernels.cuh"
@@ -36,39 +40,54 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kTile = 128;                  // tokens per tile (the MMA's M)
-constexpr int kVDim = 128;                  // v_head_dim
-constexpr int kColsPerCta = 64;             // the MMA's N in both phases
-constexpr uint32_t kPolls = 100000;         // suspend-hinted polls: about 2 s
+constexpr int kTile = 128;           // tokens per tile (the MMA's M)
+constexpr int kVDim = 128;           // v_head_dim
+constexpr int kCols = 64;            // the MMA's N in both phases
+constexpr uint32_t kPolls = 100000;  // suspend-hinted polls: about 2 s
 
-// phase 1 shared memory: A = 8 K blocks x 128 rows x 128 B, B = 512 K rows x 128 B
-constexpr int kP1OffA = 0;
-constexpr int kP1KBlock = kTile * 128;      // 16 KB
-constexpr int kP1OffB = 8 * kP1KBlock;      // 128 KB
-constexpr int kP1OffMbar = kP1OffB + kLatent * 128;
-constexpr int kP1Smem = kP1OffMbar + 64;
+// phase 1 shared memory
+constexpr int kP1ABlock = kTile * 128;  // one K block (64) of o's tile: 128 rows x 128 B
+constexpr int kP1BBlock = 64 * 128;     // 64 K rows of W_UV's half: 64 rows x 128 B
+constexpr int kP1OffB = 8 * kP1ABlock;
+constexpr int kP1OffBar = kP1OffB + 8 * kP1BBlock;  // full[8], dfull, abort, tmem slot
+constexpr int kP1Smem = kP1OffBar + 128;
 
-// phase 2 shared memory: W_o slice (K / 64 blocks x 64 rows x 128 B), then two
-// A stages of 2 K blocks x 128 rows x 128 B
-constexpr int kP2WBlock = kColsPerCta * 128;  // 8 KB per 64 K
-constexpr int kP2Stage = 2 * kP1KBlock;       // 32 KB: K = 128 of 128 rows
+// phase 2 shared memory: W_o slice (K / 64 blocks of 64 rows x 128 B), then
+// the x ring, then the barriers
+constexpr int kP2WBlock = kCols * 128;  // 8 KB
+constexpr int kP2Stages = 6;
+constexpr int kP2Stage = kTile * 128;   // 16 KB: K = 64 of 128 token rows
 constexpr int kP2MaxK = 1024;
+constexpr int kP2TmemCols = 2 * kCols;  // two accumulators
 
-__host__ __device__ constexpr int p2_off_a(int k) { return (k / 64) * kP2WBlock; }
-__host__ __device__ constexpr int p2_off_mbar(int k) { return p2_off_a(k) + 2 * kP2Stage; }
-__host__ __device__ constexpr int p2_smem(int k) { return p2_off_mbar(k) + 64; }
+__host__ __device__ constexpr int p2_off_ring(int k) { return (k / 64) * kP2WBlock; }
+__host__ __device__ constexpr int p2_off_bar(int k) { return p2_off_ring(k) + kP2Stages * kP2Stage; }
+__host__ __device__ constexpr int p2_smem(int k) { return p2_off_bar(k) + 256; }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
+struct P2Bars {
+  uint64_t w_full;
+  uint64_t a_full[kP2Stages];
+  uint64_t a_empty[kP2Stages];
+  uint64_t d_full[2];
+  uint64_t d_empty[2];
+  int abort;
+  uint32_t tmem;
+};
+static_assert(sizeof(P2Bars) <= 256, "phase 2 barrier block");
+
+__device__ __forceinline__ void arrive1(uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(mbar)) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+
+// bounded wait that also ends when another role has given up; gives up itself
+// by raising the flag
+__device__ __forceinline__ bool wait_or_abort(uint64_t* mbar, uint32_t parity, volatile int* abort) {
+  if (mbar_wait_or_abort(mbar, parity, kPolls, abort)) return true;
+  *abort = 1;
+  return false;
 }
 
-// fp32 TMEM columns [col, col + 32) of this thread's lane -> 32 bf16 at dst (64 B)
+// fp32 TMEM columns of this thread's lane -> 32 bf16 at dst (64 B)
 __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const uint32_t (&v)[32]) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -87,10 +106,13 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const uint32_t
 // ---------------------------------------------------------------------------
 // phase 1: x[tile, h*128 + 64 z ..] = bf16(o[h, tile, :] @ W_UV[h][:, 64 z ..])
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256, 1) v_up_kernel(const __grid_constant__ VUpOProjArgs a) {
+__global__ void __launch_bounds__(256, 1)
+    v_up_kernel(const __grid_constant__ VUpOProjArgs a, const __grid_constant__ VUpOProjMaps maps) {
   extern __shared__ __align__(1024) uint8_t sm[];
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kP1OffMbar);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kP1OffMbar + 8);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kP1OffBar);  // [8]
+  uint64_t* dfull = full + 8;
+  volatile int* abort = reinterpret_cast<volatile int*>(full + 9);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 10);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, t0 = blockIdx.y * kTile, z = blockIdx.z;
   const int ntok = min(kTile, a.num_tokens - t0);
@@ -98,184 +120,177 @@ __global__ void __launch_bounds__(256, 1) v_up_kernel(const __grid_constant__ VU
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
   if (tid == 0) {
-    mbar_init(mbar, 1);
+    for (int i = 0; i < 9; ++i) mbar_init(&full[i], 1);
+    *abort = 0;
     fence_mbar_init();
+    prefetch_tensormap(&maps.o);
+    prefetch_tensormap(&maps.w_uv);
+#pragma unroll 1
+    for (int kb = 0; kb < 8; ++kb) {
+      mbar_arrive_expect_tx(&full[kb], kP1ABlock + kP1BBlock);
+      tma_load_3d(sm + kb * kP1ABlock, &maps.o, 64 * kb, t0, h, &full[kb]);
+      tma_load_2d(sm + kP1OffB + kb * kP1BBlock, &maps.w_uv, kCols * z, h * kLatent + 64 * kb, &full[kb]);
+    }
   }
-  if (warp == 0) tmem_alloc(tslot, kColsPerCta);
-  // A: token r, 16-byte chunk c of its 512 latent elements (c / 8 = K block)
-  const __nv_bfloat16* o = a.o + h * a.o_stride_h;
-  for (int i = tid; i < kTile * 64; i += 256) {
-    const int r = i >> 6, c = i & 63;
-    const int rr = r < ntok ? r : 0;  // rows past the tokens read row 0's address and write zeros
-    cp_async16(sm + kP1OffA + (c >> 3) * kP1KBlock + (r >> 3) * 1024 + sw128_offset(r & 7, c & 7),
-               o + (t0 + rr) * a.o_stride_t + 8 * c, r < ntok ? 16u : 0u);
-  }
-  // B: K row k, 16-byte chunk c of this CTA's 64 columns of W_UV[h]
-  const __nv_bfloat16* w = a.w_uv + static_cast<int64_t>(h) * kLatent * kVDim + kColsPerCta * z;
-  for (int i = tid; i < kLatent * 8; i += 256) {
-    const int k = i >> 3, c = i & 7;
-    cp_async16(sm + kP1OffB + (k >> 3) * 1024 + sw128_offset(k & 7, c), w + k * kVDim + 8 * c, 16u);
-  }
-  asm volatile("cp.async.wait_all;\n" ::: "memory");
-  fence_proxy_async_smem();
+  if (warp == 0) tmem_alloc(tslot, kCols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tslot;
 
   if (tid == 0) {
-    const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, true, kTile, kColsPerCta);
-    const uint64_t da = smem_desc(smem_addr(sm + kP1OffA), 16, 1024, kSwizzle128B);
-    const uint64_t db = smem_desc(smem_addr(sm + kP1OffB), kLatent * 128, 1024, kSwizzle128B);
+    const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, true, kTile, kCols);
+    const uint64_t da = smem_desc(smem_addr(sm), 16, 1024, kSwizzle128B);
+    const uint64_t db = smem_desc(smem_addr(sm + kP1OffB), 8 * kP1BBlock, 1024, kSwizzle128B);
+#pragma unroll 1
+    for (int kb = 0; kb < 8; ++kb) {
+      if (!wait_or_abort(&full[kb], 0, abort)) break;
+      fence_after_sync();
 #pragma unroll
-    for (int k = 0; k < kLatent / 16; ++k)
-      mma_f16_ss(tmem, da + (((k >> 2) * kP1KBlock + (k & 3) * 32) >> 4), db + ((k * 2048) >> 4), idesc,
-                 k > 0 ? 1u : 0u);
-    mma_commit(mbar);
+      for (int j = 0; j < 4; ++j)  // K step 4 kb + j: 32 B into A's rows, 16 rows (2 KB) into B
+        mma_f16_ss(tmem, da + ((kb * kP1ABlock + j * 32) >> 4), db + ((kb * kP1BBlock + j * 2048) >> 4), idesc,
+                   (kb > 0 || j > 0) ? 1u : 0u);
+    }
+    mma_commit(dfull);  // arrives at once when no MMA was issued
   }
   // warp-uniform, as the TMEM load below is a warp-wide instruction
-  const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(mbar, 0, kPolls));
+  const bool done = __all_sync(0xffffffffu, wait_or_abort(dfull, 0, abort) && *abort == 0);
   fence_after_sync();
   const int q = warp & 3, half = warp >> 2, r = 32 * q + lane;
   if (done) {
     uint32_t v[32];
     tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + 32 * half, v);
     tmem_ld_wait();
-    if (r < ntok)
-      store_bf16x32(a.x + static_cast<int64_t>(t0 + r) * a.num_heads * kVDim + h * kVDim + kColsPerCta * z + 32 * half,
-                    v);
+    if (r < ntok) {
+      store_bf16x32(a.x + static_cast<int64_t>(t0 + r) * a.num_heads * kVDim + h * kVDim + kCols * z + 32 * half, v);
+      // the o_proj grid reads x through the async proxy (TMA)
+      asm volatile("fence.proxy.async.global;\n" ::: "memory");
+    }
   }
   fence_before_sync();
   __syncthreads();
   if (warp == 0) {
     fence_after_sync();
-    tmem_dealloc(tmem, kColsPerCta);
+    tmem_dealloc(tmem, kCols);
   }
 }
 
 // ---------------------------------------------------------------------------
 // phase 2: out[:, n0 .. n0 + 63] = bf16(x @ W_o[n0 .. n0 + 63, :]^T)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256, 1) o_proj_kernel(const __grid_constant__ VUpOProjArgs a) {
+__global__ void __launch_bounds__(256, 1)
+    o_proj_kernel(const __grid_constant__ VUpOProjArgs a, const __grid_constant__ VUpOProjMaps maps) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int K = a.num_heads * kVDim;
-  const int off_a = p2_off_a(K);
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + p2_off_mbar(K));  // [2]: one per A stage
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + p2_off_mbar(K) + 16);
+  const int kblocks = K / 64;  // x chunks per token tile = W_o blocks
+  P2Bars* bars = reinterpret_cast<P2Bars*>(sm + p2_off_bar(K));
+  volatile int* abort = &bars->abort;
+  uint8_t* ring = sm + p2_off_ring(K);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kColsPerCta;
-  const int kchunks = K / 128, chunks16 = K / 8;  // K chunks of the A ring; 16-byte chunks per W_o row
+  const int n0 = blockIdx.x * kCols;
+  const int tiles = (a.num_tokens + kTile - 1) / kTile;
+  const int total = tiles * kblocks;
 
   if (tid == 0) {
-    mbar_init(&mbar[0], 1);
-    mbar_init(&mbar[1], 1);
+    mbar_init(&bars->w_full, 1);
+    for (int s = 0; s < kP2Stages; ++s) {
+      mbar_init(&bars->a_full[s], 1);
+      mbar_init(&bars->a_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->d_full[b], 1);
+      mbar_init(&bars->d_empty[b], 128);
+    }
+    bars->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(tslot, kColsPerCta);
-  // W_o rows n0 .. n0 + 63 (K-major: row n, 16-byte chunk c along K), issued
-  // before the dependency wait -- nothing here depends on phase 1
-  const __nv_bfloat16* w = a.w_o + static_cast<int64_t>(n0) * K;
-  for (int i = tid; i < kColsPerCta * chunks16; i += 256) {
-    const int n = i / chunks16, c = i - n * chunks16;
-    cp_async16(sm + (c >> 3) * kP2WBlock + (n >> 3) * 1024 + sw128_offset(n & 7, c & 7), w + n * K + 8 * c, 16u);
-  }
-  cp_async_commit();
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");  // phase 1 complete, x visible
-
-  const int tiles = (a.num_tokens + kTile - 1) / kTile;
-  const int total = tiles * kchunks;  // A chunks over all token tiles, in order
-  // A chunk g (token tile g / kchunks, K columns 128 (g % kchunks) ..) into stage g % 2
-  auto load_a = [&](int g) {
-    const int t0 = (g / kchunks) * kTile, kc = g % kchunks;
-    const int ntok = min(kTile, a.num_tokens - t0);
-    uint8_t* st = sm + off_a + (g & 1) * kP2Stage;
-    for (int i = tid; i < kTile * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      const int rr = r < ntok ? r : 0;
-      cp_async16(st + (c >> 3) * kP1KBlock + (r >> 3) * 1024 + sw128_offset(r & 7, c & 7),
-                 a.x + static_cast<int64_t>(t0 + rr) * K + 128 * kc + 8 * c, r < ntok ? 16u : 0u);
-    }
-    cp_async_commit();
-  };
-  load_a(0);
-  if (total > 1) load_a(1);
+  if (warp == 0) tmem_alloc(&bars->tmem, kP2TmemCols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  const uint32_t tmem = *tslot;
-  const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, false, kTile, kColsPerCta);
-  const uint64_t dw = smem_desc(smem_addr(sm), 16, 1024, kSwizzle128B);
-  bool ok = true;
-  uint32_t parity = 0u;  // bit s: parity of stage s's next commit (its commits so far, mod 2)
+  const uint32_t tmem = bars->tmem;
 
-  for (int g = 0; g < total; ++g) {
-    const int kc = g % kchunks, s = g & 1;
-    // this thread's copies of chunk g (and the weights) have landed
-    if (g + 1 < total)
-      cp_async_wait<1>();
-    else
-      cp_async_wait<0>();
-    fence_proxy_async_smem();
-    fence_before_sync();
-    __syncthreads();  // everyone's copies
+  if (warp == 0 && lane == 0) {
+    // ---- producer: the weights (no dependency on phase 1), then the x ring ----
+    prefetch_tensormap(&maps.w_o);
+    prefetch_tensormap(&maps.x);
+    mbar_arrive_expect_tx(&bars->w_full, static_cast<uint32_t>(kblocks * kP2WBlock));
+#pragma unroll 1
+    for (int kb = 0; kb < kblocks; ++kb) tma_load_2d(sm + kb * kP2WBlock, &maps.w_o, 64 * kb, n0, &bars->w_full);
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");  // phase 1 complete, x written
+#pragma unroll 1
+    for (int g = 0; g < total; ++g) {
+      const int s = g % kP2Stages;
+      if (g >= kP2Stages && !wait_or_abort(&bars->a_empty[s], ((g / kP2Stages) - 1) & 1, abort)) break;
+      mbar_arrive_expect_tx(&bars->a_full[s], kP2Stage);
+      tma_load_2d(ring + s * kP2Stage, &maps.x, 64 * (g % kblocks), (g / kblocks) * kTile, &bars->a_full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issue ----
+    const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, false, kTile, kCols);
+    const uint64_t dw = smem_desc(smem_addr(sm), 16, 1024, kSwizzle128B);
+    bool ok = wait_or_abort(&bars->w_full, 0, abort);
     fence_after_sync();
-    if (tid == 0) {
-      const uint64_t da = smem_desc(smem_addr(sm + off_a + s * kP2Stage), 16, 1024, kSwizzle128B);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int kk = 8 * kc + k;  // K step of 16 over the whole row
-        mma_f16_ss(tmem, da + (((k >> 2) * kP1KBlock + (k & 3) * 32) >> 4),
-                   dw + (((kk >> 2) * kP2WBlock + (kk & 3) * 32) >> 4), idesc, (kc > 0 || k > 0) ? 1u : 0u);
-      }
-      mma_commit(&mbar[s]);
-    }
-    const bool last_of_tile = kc == kchunks - 1;
-    if (g + 2 < total || last_of_tile) {
-      // stage s is rewritten next (chunk g + 2), or the tile's D is read: wait
-      // for this chunk's MMAs (commits complete in order)
-      ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&mbar[s], (parity >> s) & 1u, kPolls));
+#pragma unroll 1
+    for (int i = 0; ok && i < tiles; ++i) {
+      const int b = i & 1;
+      if (i >= 2 && !(ok = wait_or_abort(&bars->d_empty[b], ((i >> 1) - 1) & 1, abort))) break;
       fence_after_sync();
+#pragma unroll 1
+      for (int c = 0; c < kblocks; ++c) {
+        const int g = i * kblocks + c, s = g % kP2Stages;
+        if (!(ok = wait_or_abort(&bars->a_full[s], (g / kP2Stages) & 1, abort))) break;
+        fence_after_sync();
+        const uint64_t da = smem_desc(smem_addr(ring + s * kP2Stage), 16, 1024, kSwizzle128B);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_f16_ss(tmem + b * kCols, da + ((j * 32) >> 4), dw + ((c * kP2WBlock + j * 32) >> 4), idesc,
+                     (c > 0 || j > 0) ? 1u : 0u);
+        mma_commit(&bars->a_empty[s]);  // the stage is free once these MMAs have read it
+      }
+      if (ok) mma_commit(&bars->d_full[b]);
     }
-    parity ^= 1u << s;
-    if (last_of_tile) {
-      const int t0 = (g / kchunks) * kTile, ntok = min(kTile, a.num_tokens - t0);
-      const int q = warp & 3, half = warp >> 2, r = 32 * q + lane;
-      if (ok) {
+  } else if (warp >= 4) {
+    // ---- epilogue: lanes 32 (warp % 4) .. + 31 of the accumulator ----
+    const int q = warp & 3, r = 32 * q + lane;
+#pragma unroll 1
+    for (int i = 0; i < tiles; ++i) {
+      const int b = i & 1, t0 = i * kTile, ntok = min(kTile, a.num_tokens - t0);
+      if (!__all_sync(0xffffffffu, wait_or_abort(&bars->d_full[b], (i >> 1) & 1, abort))) break;
+      fence_after_sync();
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t v[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + 32 * half, v);
+        tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + b * kCols + 32 * h2, v);
         tmem_ld_wait();
-        if (r < ntok) store_bf16x32(a.out + static_cast<int64_t>(t0 + r) * a.out_stride + n0 + 32 * half, v);
+        if (r < ntok) store_bf16x32(a.out + static_cast<int64_t>(t0 + r) * a.out_stride + n0 + 32 * h2, v);
       }
       fence_before_sync();
-      __syncthreads();  // D read before the next tile's first MMA overwrites it
-      fence_after_sync();
+      arrive1(&bars->d_empty[b]);  // this accumulator may take tile i + 2
     }
-    if (g + 2 < total) load_a(g + 2);
   }
   fence_before_sync();
   __syncthreads();
   if (warp == 0) {
     fence_after_sync();
-    tmem_dealloc(tmem, kColsPerCta);
+    tmem_dealloc(tmem, kP2TmemCols);
   }
 }
 
 }  // namespace
 
-int v_up_o_proj_max_k() { return kP2MaxK; }
-
-cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, cudaStream_t stream) {
+cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, const VUpOProjMaps& maps, cudaStream_t stream) {
   const int K = a.num_heads * kVDim;
   cudaError_t e = cudaFuncSetAttribute(v_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP1Smem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(o_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p2_smem(kP2MaxK));
   if (e != cudaSuccess) return e;
-  const dim3 grid1(a.num_heads, (a.num_tokens + kTile - 1) / kTile, kVDim / kColsPerCta);
-  v_up_kernel<<<grid1, 256, kP1Smem, stream>>>(a);
+  const dim3 grid1(a.num_heads, (a.num_tokens + kTile - 1) / kTile, kVDim / kCols);
+  v_up_kernel<<<grid1, 256, kP1Smem, stream>>>(a, maps);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.hidden / kColsPerCta);
+  cfg.gridDim = dim3(a.hidden / kCols);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = p2_smem(K);
   cfg.stream = stream;
@@ -284,7 +299,7 @@ cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, o_proj_kernel, a);
+  return cudaLaunchKernelEx(&cfg, o_proj_kernel, a, maps);
 }
 
 }  // namespace kimi

@@ -14,29 +14,22 @@
 // Two launches on one stream, the second a programmatic dependent of the
 // first.  Every operand arrives by TMA (tiled, 128-byte swizzle: the UMMA
 // operand layout; no multicast) on mbarriers:
-//   * phase 1, a cluster of 4 CTAs per (head, 128-token tile, 64-column half
-//     of V), one per quarter of the 512-long contraction: each CTA loads its
-//     2 K blocks of o's tile (A, K-major) and of W_UV's half (B, MN-major as
-//     stored), 48 KB in all, and accumulates a partial with tcgen05.mma
-//     kind::f16 (M = 128 tokens, N = 64, K = 16); the partials go to shared
-//     memory, and CTA q of the cluster sums the four (in quarter order, over
-//     distributed shared memory) for tokens 32 q .. 32 q + 31 and writes x as
-//     bf16 to a scratch [T, H * 128] that stays in L2 -- 64 CTAs pull the
-//     2 MB of o and W_UV at the Kimi-K2 TP8 shape instead of 16;
+//   * phase 1, one CTA per (head, 128-token tile, 64-column half of V): the 8
+//     K blocks of o's tile (A, K-major, 16 KB each) and of W_UV's half (B,
+//     MN-major as stored, 8 KB each) are all requested at once, one mbarrier
+//     per K block, and the MMAs of a block (tcgen05.mma kind::f16, M = 128
+//     tokens, N = 64, K = 16) issue as soon as it lands; x is written as bf16
+//     to a scratch [T, H * 128] that stays in L2;
 //   * phase 2, one CTA per 64 outputs of the hidden dimension, warp roles:
 //     warp 0 lane 0 loads the CTA's whole W_o slice (64 x H * 128, at most
-//     128 KB, resident; one mbarrier per 64-wide K block) BEFORE waiting for
-//     phase 1 (griddepcontrol.wait), so the weight stream -- the step's HBM
-//     traffic -- overlaps phase 1, then streams x through a ring of six 16 KB
-//     stages (K = 64 each); warp 1 lane 0 issues the MMAs (M = 128 tokens,
-//     N = 64) into one of two TMEM accumulators; warps 4-7 read a finished
-//     accumulator and write out while the next token tile accumulates in the
-//     other.  Each CTA walks the K blocks starting at its own offset
-//     (blockIdx.x mod K / 64), so the 112 CTAs do not all request the same x
-//     lines at the same moment.
+//     128 KB, resident) BEFORE waiting for phase 1 (griddepcontrol.wait), so
+//     the weight stream -- the step's HBM traffic -- overlaps phase 1, then
+//     streams x through a ring of six 16 KB stages (K = 64 each); warp 1
+//     lane 0 issues the MMAs (M = 128 tokens, N = 64) into one of two TMEM
+//     accumulators; warps 4-7 read a finished accumulator and write out while
+//     the next token tile accumulates in the other.
 // Every wait is bounded; a give-up raises a shared abort flag that ends the
 // other roles' waits, and leaves the output unwritten or partly written.
-#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "kernels.cuh"
@@ -52,14 +45,12 @@ constexpr int kVDim = 128;           // v_head_dim
 constexpr int kCols = 64;            // the MMA's N in both phases
 constexpr uint32_t kPolls = 100000;  // suspend-hinted polls: about 2 s
 
-// phase 1 shared memory (per CTA: one quarter of the contraction, 128 long)
-constexpr int kP1Split = 4;             // CTAs per cluster
+// phase 1 shared memory
 constexpr int kP1ABlock = kTile * 128;  // one K block (64) of o's tile: 128 rows x 128 B
 constexpr int kP1BBlock = 64 * 128;     // 64 K rows of W_UV's half: 64 rows x 128 B
-constexpr int kP1OffB = 2 * kP1ABlock;
-constexpr int kP1OffPart = kP1OffB + 2 * kP1BBlock;  // fp32 partial [64 cols][128 tokens]
-constexpr int kP1OffBar = kP1OffPart + kCols * kTile * 4;  // full, dfull, abort, tmem slot
-constexpr int kP1Smem = kP1OffBar + 64;
+constexpr int kP1OffB = 8 * kP1ABlock;
+constexpr int kP1OffBar = kP1OffB + 8 * kP1BBlock;  // full[8], dfull, abort, tmem slot
+constexpr int kP1Smem = kP1OffBar + 128;
 
 // phase 2 shared memory: W_o slice (K / 64 blocks of 64 rows x 128 B), then
 // the x ring, then the barriers
@@ -71,10 +62,10 @@ constexpr int kP2TmemCols = 2 * kCols;  // two accumulators
 
 __host__ __device__ constexpr int p2_off_ring(int k) { return (k / 64) * kP2WBlock; }
 __host__ __device__ constexpr int p2_off_bar(int k) { return p2_off_ring(k) + kP2Stages * kP2Stage; }
-__host__ __device__ constexpr int p2_smem(int k) { return p2_off_bar(k) + 512; }
+__host__ __device__ constexpr int p2_smem(int k) { return p2_off_bar(k) + 256; }
 
 struct P2Bars {
-  uint64_t w_full[kP2MaxK / 64];  // one per 64-wide K block of the weights
+  uint64_t w_full;
   uint64_t a_full[kP2Stages];
   uint64_t a_empty[kP2Stages];
   uint64_t d_full[2];
@@ -82,7 +73,7 @@ struct P2Bars {
   int abort;
   uint32_t tmem;
 };
-static_assert(sizeof(P2Bars) <= 512, "phase 2 barrier block");
+static_assert(sizeof(P2Bars) <= 256, "phase 2 barrier block");
 
 __device__ __forceinline__ void arrive1(uint64_t* mbar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(mbar)) : "memory");
@@ -113,39 +104,32 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const uint32_t
 }
 
 // ---------------------------------------------------------------------------
-// phase 1: x[tile, h*128 + 64 z ..] = bf16(o[h, tile, :] @ W_UV[h][:, 64 z ..]),
-// the contraction split over the 4 CTAs of a cluster
+// phase 1: x[tile, h*128 + 64 z ..] = bf16(o[h, tile, :] @ W_UV[h][:, 64 z ..])
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256, 1)
     v_up_kernel(const __grid_constant__ VUpOProjArgs a, const __grid_constant__ VUpOProjMaps maps) {
-  namespace cg = cooperative_groups;
   extern __shared__ __align__(1024) uint8_t sm[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kP1OffBar);
-  uint64_t* dfull = full + 1;
-  volatile int* abort = reinterpret_cast<volatile int*>(full + 2);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 3);
-  float* part = reinterpret_cast<float*>(sm + kP1OffPart);
-  cg::cluster_group cluster = cg::this_cluster();
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kP1OffBar);  // [8]
+  uint64_t* dfull = full + 8;
+  volatile int* abort = reinterpret_cast<volatile int*>(full + 9);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 10);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kq = static_cast<int>(cluster.block_rank());  // quarter of the contraction
-  const int h = blockIdx.x / kP1Split, t0 = blockIdx.y * kTile, z = blockIdx.z;
+  const int h = blockIdx.x, t0 = blockIdx.y * kTile, z = blockIdx.z;
   const int ntok = min(kTile, a.num_tokens - t0);
   // the o_proj grid may start now: its prologue reads only W_o
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
   if (tid == 0) {
-    mbar_init(full, 1);
-    mbar_init(dfull, 1);
+    for (int i = 0; i < 9; ++i) mbar_init(&full[i], 1);
     *abort = 0;
     fence_mbar_init();
     prefetch_tensormap(&maps.o);
     prefetch_tensormap(&maps.w_uv);
-    mbar_arrive_expect_tx(full, 2 * (kP1ABlock + kP1BBlock));
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int k0 = 128 * kq + 64 * j;
-      tma_load_3d(sm + j * kP1ABlock, &maps.o, k0, t0, h, full);
-      tma_load_2d(sm + kP1OffB + j * kP1BBlock, &maps.w_uv, kCols * z, h * kLatent + k0, full);
+#pragma unroll 1
+    for (int kb = 0; kb < 8; ++kb) {
+      mbar_arrive_expect_tx(&full[kb], kP1ABlock + kP1BBlock);
+      tma_load_3d(sm + kb * kP1ABlock, &maps.o, 64 * kb, t0, h, &full[kb]);
+      tma_load_2d(sm + kP1OffB + kb * kP1BBlock, &maps.w_uv, kCols * z, h * kLatent + 64 * kb, &full[kb]);
     }
   }
   if (warp == 0) tmem_alloc(tslot, kCols);
@@ -157,13 +141,15 @@ __global__ void __launch_bounds__(256, 1)
   if (tid == 0) {
     const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, true, kTile, kCols);
     const uint64_t da = smem_desc(smem_addr(sm), 16, 1024, kSwizzle128B);
-    const uint64_t db = smem_desc(smem_addr(sm + kP1OffB), 2 * kP1BBlock, 1024, kSwizzle128B);
-    if (wait_or_abort(full, 0, abort)) {
+    const uint64_t db = smem_desc(smem_addr(sm + kP1OffB), 8 * kP1BBlock, 1024, kSwizzle128B);
+#pragma unroll 1
+    for (int kb = 0; kb < 8; ++kb) {
+      if (!wait_or_abort(&full[kb], 0, abort)) break;
       fence_after_sync();
 #pragma unroll
-      for (int k = 0; k < 8; ++k)  // K step k: 32 B into A's rows of block k / 4, 16 rows (2 KB) into B
-        mma_f16_ss(tmem, da + (((k >> 2) * kP1ABlock + (k & 3) * 32) >> 4), db + ((k * 2048) >> 4), idesc,
-                   k > 0 ? 1u : 0u);
+      for (int j = 0; j < 4; ++j)  // K step 4 kb + j: 32 B into A's rows, 16 rows (2 KB) into B
+        mma_f16_ss(tmem, da + ((kb * kP1ABlock + j * 32) >> 4), db + ((kb * kP1BBlock + j * 2048) >> 4), idesc,
+                   (kb > 0 || j > 0) ? 1u : 0u);
     }
     mma_commit(dfull);  // arrives at once when no MMA was issued
   }
@@ -175,46 +161,14 @@ __global__ void __launch_bounds__(256, 1)
     uint32_t v[32];
     tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + 32 * half, v);
     tmem_ld_wait();
-#pragma unroll
-    for (int c = 0; c < 32; ++c) part[(32 * half + c) * kTile + r] = __uint_as_float(v[c]);  // [col][token]
-  }
-  // every CTA's partial (or its give-up flag) is in its shared memory; a
-  // give-up anywhere in the cluster leaves the cluster's x rows unwritten
-  int* gave_up = reinterpret_cast<int*>(full + 4);
-  const int bad_here = __syncthreads_or(!done);
-  if (tid == 0) *gave_up = bad_here;
-  cluster.sync();
-  int bad = 0;
-#pragma unroll
-  for (int src = 0; src < kP1Split; ++src) bad |= *cluster.map_shared_rank(gave_up, src);
-  {
-    // tokens 32 kq + (tid % 32), columns 8 (tid / 32) .. + 7: the four
-    // partials summed in quarter order
-    const int row = 32 * kq + lane, cg8 = warp;
-    float acc[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
-#pragma unroll
-    for (int src = 0; src < kP1Split; ++src) {
-      const float* rp = cluster.map_shared_rank(part, src);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = src == 0 ? rp[(8 * cg8 + c) * kTile + row]
-                                                    : __fadd_rn(acc[c], rp[(8 * cg8 + c) * kTile + row]);
-    }
-    if (!bad && row < ntok) {
-      uint32_t p[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat162 pr = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
-        p[e] = *reinterpret_cast<const uint32_t*>(&pr);
-      }
-      *reinterpret_cast<uint4*>(a.x + static_cast<int64_t>(t0 + row) * a.num_heads * kVDim + h * kVDim + kCols * z +
-                                8 * cg8) = make_uint4(p[0], p[1], p[2], p[3]);
+    if (r < ntok) {
+      store_bf16x32(a.x + static_cast<int64_t>(t0 + r) * a.num_heads * kVDim + h * kVDim + kCols * z + 32 * half, v);
       // the o_proj grid reads x through the async proxy (TMA)
       asm volatile("fence.proxy.async.global;\n" ::: "memory");
     }
   }
-  cluster.sync();  // no CTA leaves while another reads its partial
+  fence_before_sync();
+  __syncthreads();
   if (warp == 0) {
     fence_after_sync();
     tmem_dealloc(tmem, kCols);
@@ -236,10 +190,9 @@ __global__ void __launch_bounds__(256, 1)
   const int n0 = blockIdx.x * kCols;
   const int tiles = (a.num_tokens + kTile - 1) / kTile;
   const int total = tiles * kblocks;
-  const int rot = blockIdx.x % kblocks;  // this CTA's first K block
 
   if (tid == 0) {
-    for (int kb = 0; kb < kblocks; ++kb) mbar_init(&bars->w_full[kb], 1);
+    mbar_init(&bars->w_full, 1);
     for (int s = 0; s < kP2Stages; ++s) {
       mbar_init(&bars->a_full[s], 1);
       mbar_init(&bars->a_empty[s], 1);
@@ -261,26 +214,23 @@ __global__ void __launch_bounds__(256, 1)
     // ---- producer: the weights (no dependency on phase 1), then the x ring ----
     prefetch_tensormap(&maps.w_o);
     prefetch_tensormap(&maps.x);
+    mbar_arrive_expect_tx(&bars->w_full, static_cast<uint32_t>(kblocks * kP2WBlock));
 #pragma unroll 1
-    for (int c = 0; c < kblocks; ++c) {  // in the order the MMAs use them
-      const int kb = (c + rot) % kblocks;
-      mbar_arrive_expect_tx(&bars->w_full[kb], kP2WBlock);
-      tma_load_2d(sm + kb * kP2WBlock, &maps.w_o, 64 * kb, n0, &bars->w_full[kb]);
-    }
+    for (int kb = 0; kb < kblocks; ++kb) tma_load_2d(sm + kb * kP2WBlock, &maps.w_o, 64 * kb, n0, &bars->w_full);
     asm volatile("griddepcontrol.wait;\n" ::: "memory");  // phase 1 complete, x written
 #pragma unroll 1
     for (int g = 0; g < total; ++g) {
       const int s = g % kP2Stages;
-      const int kb = (g % kblocks + rot) % kblocks;
       if (g >= kP2Stages && !wait_or_abort(&bars->a_empty[s], ((g / kP2Stages) - 1) & 1, abort)) break;
       mbar_arrive_expect_tx(&bars->a_full[s], kP2Stage);
-      tma_load_2d(ring + s * kP2Stage, &maps.x, 64 * kb, (g / kblocks) * kTile, &bars->a_full[s]);
+      tma_load_2d(ring + s * kP2Stage, &maps.x, 64 * (g % kblocks), (g / kblocks) * kTile, &bars->a_full[s]);
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issue ----
     const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, false, kTile, kCols);
     const uint64_t dw = smem_desc(smem_addr(sm), 16, 1024, kSwizzle128B);
-    bool ok = true;
+    bool ok = wait_or_abort(&bars->w_full, 0, abort);
+    fence_after_sync();
 #pragma unroll 1
     for (int i = 0; ok && i < tiles; ++i) {
       const int b = i & 1;
@@ -288,14 +238,13 @@ __global__ void __launch_bounds__(256, 1)
       fence_after_sync();
 #pragma unroll 1
       for (int c = 0; c < kblocks; ++c) {
-        const int g = i * kblocks + c, s = g % kP2Stages, kb = (c + rot) % kblocks;
-        if (i == 0 && !(ok = wait_or_abort(&bars->w_full[kb], 0, abort))) break;
+        const int g = i * kblocks + c, s = g % kP2Stages;
         if (!(ok = wait_or_abort(&bars->a_full[s], (g / kP2Stages) & 1, abort))) break;
         fence_after_sync();
         const uint64_t da = smem_desc(smem_addr(ring + s * kP2Stage), 16, 1024, kSwizzle128B);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          mma_f16_ss(tmem + b * kCols, da + ((j * 32) >> 4), dw + ((kb * kP2WBlock + j * 32) >> 4), idesc,
+          mma_f16_ss(tmem + b * kCols, da + ((j * 32) >> 4), dw + ((c * kP2WBlock + j * 32) >> 4), idesc,
                      (c > 0 || j > 0) ? 1u : 0u);
         mma_commit(&bars->a_empty[s]);  // the stage is free once these MMAs have read it
       }
@@ -336,22 +285,10 @@ cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, const VUpOProjMaps& maps, 
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(o_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p2_smem(kP2MaxK));
   if (e != cudaSuccess) return e;
-  {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kP1Split * a.num_heads, (a.num_tokens + kTile - 1) / kTile, kVDim / kCols);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = kP1Smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kP1Split;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, v_up_kernel, a, maps);
-    if (e != cudaSuccess) return e;
-  }
+  const dim3 grid1(a.num_heads, (a.num_tokens + kTile - 1) / kTile, kVDim / kCols);
+  v_up_kernel<<<grid1, 256, kP1Smem, stream>>>(a, maps);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.hidden / kCols);
   cfg.blockDim = dim3(256);

@@ -504,7 +504,7 @@ int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* p, void* stream) {
   kimi::VUpOProjMaps maps;
   {
     const cuuint64_t dims[3] = {512, T, H}, strides[2] = {stride_t, stride_h};
-    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kimi::kVUpRows), 1};
     if (!encode_bf16_map(maps.o, p->o, 3, dims, strides, box)) return KIMI_ERR_BAD_STRIDE;
   }
   {

@@ -103,6 +103,9 @@ struct VUpOProjArgs {
 // swizzle: o as [H][T][512] (box 64 x 128 tokens x 1 head), W_UV as
 // [H * 512][128] (box 64 x 64 rows), x as [T][H * 128] (box 64 x 128 tokens),
 // W_o as [hidden][H * 128] (box 64 x 64 rows).
+// Tokens per phase-1 CTA of the V up-projection (the o map's box height).
+constexpr int kVUpRows = 64;
+
 struct VUpOProjMaps {
   CUtensorMap o;
   CUtensorMap w_uv;

@@ -14,12 +14,12 @@
 // Two launches on one stream, the second a programmatic dependent of the
 // first.  Every operand arrives by TMA (tiled, 128-byte swizzle: the UMMA
 // operand layout; no multicast) on mbarriers:
-//   * phase 1, one CTA per (head, 128-token tile, 64-column half of V): the 8
-//     K blocks of o's tile (A, K-major, 16 KB each) and of W_UV's half (B,
-//     MN-major as stored, 8 KB each) are all requested at once, one mbarrier
-//     per K block, and the MMAs of a block (tcgen05.mma kind::f16, M = 128
-//     tokens, N = 64, K = 16) issue as soon as it lands; x is written as bf16
-//     to a scratch [T, H * 128] that stays in L2;
+//   * phase 1, one CTA per (head, kVUpRows tokens, 64-column half of V): the
+//     8 K blocks of its o rows (A, K-major) and of W_UV's half (B, MN-major
+//     as stored, 8 KB each) are all requested at once, one mbarrier per K
+//     block, and the MMAs of a block (tcgen05.mma kind::f16, M = 128, N = 64,
+//     K = 16) issue as soon as it lands; x is written as bf16 to a scratch
+//     [T, H * 128] that stays in L2;
 //   * phase 2, one CTA per 64 outputs of the hidden dimension, warp roles:
 //     warp 0 lane 0 loads the CTA's whole W_o slice (64 x H * 128, at most
 //     128 KB, resident) BEFORE waiting for phase 1 (griddepcontrol.wait), so
@@ -46,8 +46,13 @@ constexpr int kCols = 64;            // the MMA's N in both phases
 constexpr uint32_t kPolls = 100000;  // suspend-hinted polls: about 2 s
 
 // phase 1 shared memory
-constexpr int kP1ABlock = kTile * 128;  // one K block (64) of o's tile: 128 rows x 128 B
-constexpr int kP1BBlock = 64 * 128;     // 64 K rows of W_UV's half: 64 rows x 128 B
+// A CTA loads kVUpRows tokens of o; its MMA still has M = 128 and the rows
+// past them (read from whatever follows in shared memory) are computed and
+// dropped.  The A blocks are packed at kVUpRows rows.
+constexpr int kP1Rows = kVUpRows;
+static_assert(kP1Rows % 32 == 0 && kP1Rows <= kTile, "whole TMEM lane quarters");
+constexpr int kP1ABlock = kP1Rows * 128;  // one K block (64) of the CTA's o rows
+constexpr int kP1BBlock = 64 * 128;       // 64 K rows of W_UV's half: 64 rows x 128 B
 constexpr int kP1OffB = 8 * kP1ABlock;
 constexpr int kP1OffBar = kP1OffB + 8 * kP1BBlock;  // full[8], dfull, abort, tmem slot
 constexpr int kP1Smem = kP1OffBar + 128;
@@ -114,8 +119,8 @@ __global__ void __launch_bounds__(256, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(full + 9);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 10);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.x, t0 = blockIdx.y * kTile, z = blockIdx.z;
-  const int ntok = min(kTile, a.num_tokens - t0);
+  const int h = blockIdx.x, t0 = blockIdx.y * kP1Rows, z = blockIdx.z;
+  const int ntok = min(kP1Rows, a.num_tokens - t0);
   // the o_proj grid may start now: its prologue reads only W_o
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
@@ -285,7 +290,7 @@ cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, const VUpOProjMaps& maps, 
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(o_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p2_smem(kP2MaxK));
   if (e != cudaSuccess) return e;
-  const dim3 grid1(a.num_heads, (a.num_tokens + kTile - 1) / kTile, kVDim / kCols);
+  const dim3 grid1(a.num_heads, (a.num_tokens + kP1Rows - 1) / kP1Rows, kVDim / kCols);
   v_up_kernel<<<grid1, 256, kP1Smem, stream>>>(a, maps);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;

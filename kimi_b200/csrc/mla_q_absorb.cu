@@ -12,17 +12,18 @@
 // (a cos - b sin, b cos + a sin) with cos / sin [max_position, 32] float32;
 // every product and sum rounded to float32 on its own, the result to bf16.
 //
-// One CTA of 256 threads per (head h, 128-token tile, output half z), two
-// CTAs per SM:
-//   * q_nope[tile, h] (A, K-major) and columns 256 z .. 256 z + 255 of W_UK[h]
+// One CTA of 256 threads per (head h, 128-token tile, column slice z of
+// kQSplit = 8): at the Kimi-K2 TP8 shape 64 CTAs, each copying 48 KB, where
+// 2 slices per head (96 KB each) measured 10.7 us per call and 8 slices 7.7:
+//   * q_nope[tile, h] (A, K-major) and columns 64 z .. 64 z + 63 of W_UK[h]
 //     (B, MN-major: rows of output columns as the weight is stored) are
-//     copied with cp.async into 128-byte-swizzled shared memory (96 KB); one
-//     thread issues 8 tcgen05.mma kind::f16 (M = 128 tokens, N = 256,
-//     K = 16) into 256 TMEM columns;
+//     copied with cp.async into 128-byte-swizzled shared memory; one thread
+//     issues 8 tcgen05.mma kind::f16 (M = 128 tokens, N = 64, K = 16) into
+//     64 TMEM columns;
 //   * meanwhile the z = 0 CTA rotates q_pe of its tile and head, and the z = 1
 //     CTA appends its share of the tile's tokens to the cache (tokens 16 h ..
 //     by stride 16 H, 16 threads per token as in the KV-append kernel);
-//   * the epilogue reads D (lane = token) and writes its 256 columns of
+//   * the epilogue reads D (lane = token) and writes its 64 columns of
 //     q_out[..., :512] as bf16.
 // The single wait is bounded; a give-up leaves q_out's latent part unwritten.
 #include <cuda_runtime.h>
@@ -39,9 +40,13 @@ using namespace sm100;
 constexpr int kTileTokens = 128;
 constexpr int kNopeDim = 128;
 constexpr int kOffA = 0;                          // 2 K blocks x 128 rows x 128 B
-constexpr int kOffB = 2 * 128 * 128;              // 4 N blocks x 128 K rows x 128 B
+constexpr int kQSplit = 8;                        // CTAs per head, each a slice of the 512 columns
+constexpr int kQCols = kLatent / kQSplit;         // output columns per CTA (the MMA's N)
+constexpr int kQNBlocks = kQCols / 64;            // 64-column blocks of W per CTA
+static_assert(kQCols % 64 == 0 && kQCols <= 256, "N of one MMA, whole 64-column blocks");
+constexpr int kOffB = 2 * 128 * 128;              // kQNBlocks N blocks x 128 K rows x 128 B
 constexpr int kNBlock = 128 * 128;                // one 64-column block of W (16 KB)
-constexpr int kOffMbar = kOffB + 4 * kNBlock;
+constexpr int kOffMbar = kOffB + kQNBlocks * kNBlock;
 constexpr int kOffPos = kOffMbar + 64;            // the tile's 128 positions (int64)
 constexpr int kSmemQA = kOffPos + kTileTokens * 8;
 constexpr uint32_t kPolls = 100000;               // suspend-hinted polls: about 2 s
@@ -76,7 +81,7 @@ __global__ void __launch_bounds__(256, 2) mla_q_absorb_kernel(const __grid_const
     mbar_init(mbar, 1);
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(tslot, 256);
+  if (warp == 0) tmem_alloc(tslot, kQCols < 32 ? 32 : kQCols);
   int64_t* pos_s = reinterpret_cast<int64_t*>(sm + kOffPos);
   if (tid < ntok) pos_s[tid] = a.positions[t0 + tid];
 
@@ -88,10 +93,11 @@ __global__ void __launch_bounds__(256, 2) mla_q_absorb_kernel(const __grid_const
     cp_async16(sm + kOffA + (c >> 3) * (128 * 128) + (r >> 3) * 1024 + sw128_offset(r & 7, c & 7),
                a.q_nope + (t0 + rr) * a.q_nope_stride_t + h * a.q_nope_stride_h + 8 * c, r < ntok ? 16u : 0u);
   }
-  // B: K row k, 16-byte chunk c of this CTA's 256 output columns (c / 8 = N block)
-  const __nv_bfloat16* w = a.w_uk + static_cast<int64_t>(h) * kNopeDim * kLatent + 256 * z;
-  for (int i = tid; i < kNopeDim * 32; i += 256) {
-    const int k = i >> 5, c = i & 31;
+  // B: K row k, 16-byte chunk c of this CTA's kQCols output columns (c / 8 = N block)
+  const __nv_bfloat16* w = a.w_uk + static_cast<int64_t>(h) * kNopeDim * kLatent + kQCols * z;
+  constexpr int kChunks = kQCols / 8;  // 16-byte chunks per K row
+  for (int i = tid; i < kNopeDim * kChunks; i += 256) {
+    const int k = i / kChunks, c = i % kChunks;
     cp_async16(sm + kOffB + (c >> 3) * kNBlock + (k >> 3) * 1024 + sw128_offset(k & 7, c & 7), w + k * kLatent + 8 * c,
                16u);
   }
@@ -103,7 +109,7 @@ __global__ void __launch_bounds__(256, 2) mla_q_absorb_kernel(const __grid_const
   const uint32_t tmem = *tslot;
 
   if (tid == 0) {
-    const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, true, 128, 256);
+    const uint32_t idesc = instr_desc(kFmtBF16, kFmtBF16, false, true, 128, kQCols);
     const uint64_t da = smem_desc(smem_addr(sm + kOffA), 16, 1024, kSwizzle128B);
     const uint64_t db = smem_desc(smem_addr(sm + kOffB), kNBlock, 1024, kSwizzle128B);
 #pragma unroll
@@ -254,13 +260,14 @@ __global__ void __launch_bounds__(256, 2) mla_q_absorb_kernel(const __grid_const
   // ---- epilogue: D (lane = token, column = latent) -> q_out[..., :512] ----
   bool done = false;
   for (uint32_t i = 0; i < kPolls && !done; ++i) done = mbar_try_wait_sleep(mbar, 0, kWaitSleepNs);
+  done = __all_sync(0xffffffffu, done);  // warp-uniform: the TMEM load below is warp-wide
   fence_after_sync();
   const int q = warp & 3, half = warp >> 2, r = 32 * q + lane;
   if (done) {
 #pragma unroll 1
-    for (int cb = 0; cb < 4; ++cb) {
+    for (int cb = 0; cb < kQCols / 64; ++cb) {
       uint32_t v[32];
-      const int tcol = 128 * half + 32 * cb, col = 256 * z + tcol;
+      const int tcol = (kQCols / 2) * half + 32 * cb, col = kQCols * z + tcol;
       tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + tcol, v);
       tmem_ld_wait();
       if (r < ntok) {
@@ -283,7 +290,7 @@ __global__ void __launch_bounds__(256, 2) mla_q_absorb_kernel(const __grid_const
   __syncthreads();
   if (warp == 0) {
     fence_after_sync();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, kQCols < 32 ? 32 : kQCols);
   }
 }
 
@@ -292,7 +299,7 @@ __global__ void __launch_bounds__(256, 2) mla_q_absorb_kernel(const __grid_const
 cudaError_t launch_q_absorb(const QAbsorbArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(mla_q_absorb_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemQA);
   if (e != cudaSuccess) return e;
-  const dim3 grid(a.num_heads, (a.num_tokens + kTileTokens - 1) / kTileTokens, 2);
+  const dim3 grid(a.num_heads, (a.num_tokens + kTileTokens - 1) / kTileTokens, kQSplit);
   mla_q_absorb_kernel<<<grid, 256, kSmemQA, stream>>>(a);
   return cudaGetLastError();
 }

@@ -215,7 +215,7 @@ def build_workload(torch, kimi, dev, seed: int):
                 ws=ws, batch=BATCH)
 
 
-E2E_GROUP = 16  # pipelined end-to-end steps per captured graph
+E2E_GROUP = 64  # pipelined end-to-end steps per captured graph
 
 
 def run_ours(args, rank, world, local_rank):

@@ -119,3 +119,51 @@ def test_python_wrappers_reject_cpu_tensors():
     ip = torch.tensor([0, 1], dtype=torch.int32)
     with pytest.raises(ValueError):
         kimi_b200.mla_decode_fwd(q, kvb, kvs, o, None, ip, ip[:1], None)
+
+
+def test_tp8_entry_points_reject_bad_arguments_on_host():
+    """The prologue, V up-projection + o_proj and all-reduce + RMSNorm + MXFP4
+    entry points check their arguments before any launch."""
+    lib = _lib.load()
+    # decode prologue
+    assert lib.kimi_mla_q_absorb_rope_append(None, None) == -1
+    p = _lib.KimiQAbsorbParams(num_tokens=4, num_heads=0, max_position=8)
+    assert lib.kimi_mla_q_absorb_rope_append(ctypes.byref(p), None) == -2      # no heads
+    p = _lib.KimiQAbsorbParams(num_tokens=4, num_heads=8, max_position=8, is_neox=2)
+    assert lib.kimi_mla_q_absorb_rope_append(ctypes.byref(p), None) == -6      # is_neox not 0/1
+    p = _lib.KimiQAbsorbParams(num_tokens=0, num_heads=8, max_position=8)
+    assert lib.kimi_mla_q_absorb_rope_append(ctypes.byref(p), None) == 0       # nothing to do
+    p = _lib.KimiQAbsorbParams(num_tokens=4, num_heads=8, max_position=8)
+    assert lib.kimi_mla_q_absorb_rope_append(ctypes.byref(p), None) == -1      # null tensors
+    # V up-projection + o_proj
+    assert lib.kimi_mla_v_up_o_proj(None, None) == -1
+    for heads, hidden in ((9, 128), (0, 128), (8, 96), (8, 0)):
+        p = _lib.KimiVUpOProjParams(num_tokens=4, num_heads=heads, hidden=hidden)
+        assert lib.kimi_mla_v_up_o_proj(ctypes.byref(p), None) == -2, (heads, hidden)
+    p = _lib.KimiVUpOProjParams(num_tokens=0, num_heads=8, hidden=128)
+    assert lib.kimi_mla_v_up_o_proj(ctypes.byref(p), None) == 0
+    p = _lib.KimiVUpOProjParams(num_tokens=4, num_heads=8, hidden=128)
+    assert lib.kimi_mla_v_up_o_proj(ctypes.byref(p), None) == -1
+    ptrs = dict(o=0x10000, w_uv=0x20000, w_o=0x30000, x=0x40000, out=0x50000)
+    p = _lib.KimiVUpOProjParams(num_tokens=4, num_heads=8, hidden=128, o_stride_h=2048, o_stride_t=516,
+                                out_stride=128, **ptrs)
+    assert lib.kimi_mla_v_up_o_proj(ctypes.byref(p), None) == -3               # token stride % 8
+    p = _lib.KimiVUpOProjParams(num_tokens=4, num_heads=8, hidden=128, o_stride_h=2048, o_stride_t=512,
+                                out_stride=64, **ptrs)
+    assert lib.kimi_mla_v_up_o_proj(ctypes.byref(p), None) == -3               # out rows overlap
+    p = _lib.KimiVUpOProjParams(num_tokens=4, num_heads=8, hidden=128, o_stride_h=2048, o_stride_t=512,
+                                out_stride=128, **dict(ptrs, out=0x50008))
+    assert lib.kimi_mla_v_up_o_proj(ctypes.byref(p), None) == -4               # misaligned out
+    # all-reduce + residual + RMSNorm + MXFP4
+    assert lib.kimi_ar_rmsnorm_mxfp4(None, None) == -1
+    for rows, hidden, n in ((4, 48, 2), (4, 8224, 2), (4, 256, 0), (4, 256, _lib.AR_MAX_INPUTS + 1)):
+        p = _lib.KimiArRmsNormParams(rows=rows, hidden=hidden, num_inputs=n, eps=1e-6)
+        assert lib.kimi_ar_rmsnorm_mxfp4(ctypes.byref(p), None) == -2, (rows, hidden, n)
+    p = _lib.KimiArRmsNormParams(rows=4, hidden=256, num_inputs=2, eps=float("nan"))
+    assert lib.kimi_ar_rmsnorm_mxfp4(ctypes.byref(p), None) == -2
+    p = _lib.KimiArRmsNormParams(rows=0, hidden=256, num_inputs=2, eps=1e-6)
+    assert lib.kimi_ar_rmsnorm_mxfp4(ctypes.byref(p), None) == 0
+    p = _lib.KimiArRmsNormParams(rows=4, hidden=256, num_inputs=2, eps=1e-6, residual=0x1000, residual_out=0x2000,
+                                 weight=0x3000, nibbles=0x4000, scales=0x5000)
+    p.inputs[0], p.inputs[1] = 0x6000, 0x7008
+    assert lib.kimi_ar_rmsnorm_mxfp4(ctypes.byref(p), None) == -4              # misaligned partial

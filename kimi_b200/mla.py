@@ -324,7 +324,9 @@ def v_up_proj_and_o_proj(o: torch.Tensor, w_uv: torch.Tensor, w_o: torch.Tensor,
     * ``out[t] = bf16(x[t] @ w_o.T)`` (fp32 accumulation).
 
     ``o`` is the decode's heads-first output bf16 [H, T, 512] (a slice of the
-    padded heads, latent dim contiguous), ``w_uv`` bf16 [H, 512, 128] and
+    padded heads, latent dim contiguous; any head and token strides that are
+    multiples of 8 elements, so the transposed view of a token-major
+    [T, H, 512] tensor works too), ``w_uv`` bf16 [H, 512, 128] and
     ``w_o`` bf16 [hidden, H * 128] contiguous (H <= 8, hidden % 64 == 0).
     ``out`` (bf16 [T, hidden], last dim contiguous, allocated when None) is
     returned: this rank's partial of the tensor-parallel all-reduce, so it

@@ -126,3 +126,19 @@ def test_empty_and_bad_arguments():
     with pytest.raises(ValueError):  # misaligned o (token stride not a multiple of 8 elements)
         base = torch.zeros(2 * 4 * 516, dtype=torch.bfloat16, device=DEV)
         kimi_b200.v_up_proj_and_o_proj(base.as_strided((2, 4, 512), (4 * 516, 516, 1)), w_uv, w_o)
+
+
+def test_token_major_o_view():
+    """o given as the transposed view of a token-major [T, H, 512] tensor (the
+    reference's standard path layout, tests/test_mla_heads_first_e2e.py:39-48):
+    head stride 512, token stride H * 512."""
+    rng = np.random.default_rng(23)
+    H, T, hidden = 8, 100, 256
+    o_std = _bf16_np(rng, (T, H, 512))
+    w_uv, w_o = _bf16_np(rng, (H, 512, 128), 0.02), _bf16_np(rng, (hidden, H * 128), 0.02)
+    x_ref, out_ref = ovu.v_up_o_proj(o_std.transpose(1, 0, 2), w_uv, w_o)
+    x = torch.empty(T, H * 128, dtype=torch.bfloat16, device=DEV)
+    out = kimi_b200.v_up_proj_and_o_proj(_t(o_std).transpose(0, 1), _t(w_uv), _t(w_o), x=x)
+    torch.cuda.synchronize()
+    _check_x(_bits(x), x_ref)
+    _check_out(_bits(out), out_ref)

@@ -82,6 +82,45 @@ def _check_cuda(err, what):
         raise RuntimeError(f"{what} failed: CUDA error {int(err)}")
 
 
+class CudaIpc:
+    """The CUDA IPC calls :class:`PeerPartials` makes (cuda-python bindings).
+
+    ``export(ptr)`` names the allocation a device pointer lies in:
+    ``(handle bytes, offset of ptr in it)``.  ``open(handle)`` maps a peer's
+    allocation into the CURRENT device's context and returns its base address;
+    ``close(base)`` unmaps it.  ``make_current(device)`` selects the device
+    whose context the mappings go into.
+    """
+
+    def export(self, ptr: int):
+        from cuda.bindings import driver, runtime
+        err, base, _ = driver.cuMemGetAddressRange(driver.CUdeviceptr(ptr))
+        _check_cuda(err, "cuMemGetAddressRange")
+        err, handle = runtime.cudaIpcGetMemHandle(int(base))
+        _check_cuda(err, "cudaIpcGetMemHandle")
+        return bytes(handle.reserved), ptr - int(base)
+
+    def make_current(self, device: torch.device):
+        from cuda.bindings import runtime
+        err, = runtime.cudaSetDevice(device.index)
+        _check_cuda(err, "cudaSetDevice")
+
+    def open(self, raw: bytes) -> int:
+        from cuda.bindings import runtime
+        h = runtime.cudaIpcMemHandle_t()
+        h.reserved = raw
+        err, base = runtime.cudaIpcOpenMemHandle(h, runtime.cudaIpcMemLazyEnablePeerAccess)
+        _check_cuda(err, "cudaIpcOpenMemHandle")
+        return int(base)
+
+    def close(self, base: int):
+        from cuda.bindings import runtime
+        runtime.cudaIpcCloseMemHandle(base)
+
+    def synchronize(self, device: torch.device):
+        torch.cuda.synchronize(device)
+
+
 class PeerPartials:
     """One partial buffer bf16 [rows, hidden] per rank, mapped into every rank.
 
@@ -91,52 +130,49 @@ class PeerPartials:
     (the o_proj output is written there); ``ptrs`` are every rank's buffer as
     device addresses this rank's GPU reads (rank order);
     :meth:`reduce_norm_quant` runs the fused kernel over them between two
-    barriers; :meth:`close` (collective) unmaps the peers' buffers.
+    barriers; :meth:`close` (collective) unmaps the peers' buffers.  ``ipc``
+    is the IPC layer (:class:`CudaIpc` unless another is given).
     """
 
-    def __init__(self, rows: int, hidden: int, device: torch.device, group=None):
+    def __init__(self, rows: int, hidden: int, device: torch.device, group=None, ipc=None):
         import torch.distributed as dist
-        from cuda.bindings import driver, runtime
 
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         if self.world > _lib.AR_MAX_INPUTS:
             raise ValueError(f"at most {_lib.AR_MAX_INPUTS} ranks")
+        self.ipc = ipc if ipc is not None else CudaIpc()
         self.device = torch.device(device)
         self.rows, self.hidden = rows, hidden
         self.local = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=self.device)
         ptr = self.local.data_ptr()
-        # the IPC handle names the whole allocation the tensor lies in
-        err, base, _ = driver.cuMemGetAddressRange(driver.CUdeviceptr(ptr))
-        _check_cuda(err, "cuMemGetAddressRange")
-        err, handle = runtime.cudaIpcGetMemHandle(int(base))
-        _check_cuda(err, "cudaIpcGetMemHandle")
         shared = [None] * self.world
-        dist.all_gather_object(shared, (bytes(handle.reserved), ptr - int(base)), group=group)
+        dist.all_gather_object(shared, self.ipc.export(ptr), group=group)
         # open every peer's allocation with this rank's GPU current: the mapping
         # (and the peer access it enables) belongs to this GPU's context
-        err, = runtime.cudaSetDevice(self.device.index)
-        _check_cuda(err, "cudaSetDevice")
+        self.ipc.make_current(self.device)
         self._opened, self.ptrs = [], []
-        for r, (raw, offset) in enumerate(shared):
-            if r == self.rank:
-                self.ptrs.append(ptr)
-                continue
-            h = runtime.cudaIpcMemHandle_t()
-            h.reserved = raw
-            err, peer_base = runtime.cudaIpcOpenMemHandle(h, runtime.cudaIpcMemLazyEnablePeerAccess)
-            _check_cuda(err, "cudaIpcOpenMemHandle")
-            self._opened.append(peer_base)
-            self.ptrs.append(int(peer_base) + offset)
+        try:
+            for r, (raw, offset) in enumerate(shared):
+                if r == self.rank:
+                    self.ptrs.append(ptr)
+                    continue
+                base = self.ipc.open(raw)
+                self._opened.append(base)
+                self.ptrs.append(base + offset)
+        except Exception:
+            for b in self._opened:
+                self.ipc.close(b)
+            self._opened, self.ptrs = [], []
+            raise
 
     def close(self):
         """Unmap the peers' buffers (collective: call on every rank once no
         kernel reads them any more)."""
-        from cuda.bindings import runtime
-        torch.cuda.synchronize(self.device)
+        self.ipc.synchronize(self.device)
         for b in self._opened:
-            runtime.cudaIpcCloseMemHandle(b)
+            self.ipc.close(b)
         self._opened, self.ptrs = [], []
         self._barrier()
 

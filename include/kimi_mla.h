@@ -8,7 +8,10 @@
  *
  *      0                  success (KIMI_OK)
  *      negative           bad arguments, detected on the host before launch
- *      positive           a CUDA runtime error from the launch (the cudaError_t
+ *      1 .. 999           a device status word read back by kimi_device_status
+ *                         (KIMI_DEVICE_* bits: a bounded device wait gave up,
+ *                         or a page id lay outside the cache)
+ *      >= 1000            a CUDA runtime error from the launch (the cudaError_t
  *                         value plus KIMI_ERR_CUDA_BASE)
  *
  * Reference interfaces replaced (paths inside the ianye23301/kimi tree):
@@ -73,6 +76,30 @@ extern "C" {
 #define KIMI_MLA_MAX_SPLITS 64
 #define KIMI_MLA_MAX_HEADS 128
 #define KIMI_MLA_STATIC_WORKSPACE_BYTES 33554432u /* 32 MiB, see kimi_mla_decode_static_workspace */
+#define KIMI_ABI_VERSION 200
+
+/* Bits the decode kernels OR into the caller's device status word
+ * (KimiMlaDecodeParams.status).  Every device-side wait of the decode is
+ * bounded in time (KimiMlaDecodeParams.timeout_ns); a wait that runs out
+ * ends the CTA's work cleanly, leaves that CTA's part of the output unwritten
+ * and sets one of the wait bits.  The reference raises a Python exception
+ * instead (patches/atom-optimizations.patch:125-128). */
+#define KIMI_DEVICE_SOFTMAX_WAIT    0x001
+#define KIMI_DEVICE_SOFTMAX_PV_WAIT 0x002
+#define KIMI_DEVICE_EPILOGUE_WAIT   0x004
+#define KIMI_DEVICE_SCALE_WAIT      0x008
+#define KIMI_DEVICE_ISSUER_WAIT     0x010
+#define KIMI_DEVICE_ISSUER_PV_WAIT  0x020
+#define KIMI_DEVICE_CONVERTER_WAIT  0x040
+#define KIMI_DEVICE_DRAIN_WAIT      0x080
+#define KIMI_DEVICE_PRODUCER_WAIT   0x100
+/* A kv_indices entry outside [0, num_pages) (negative included): nothing
+ * is read from outside the cache; that page reads as zeros (zero keys and
+ * values, so its 64 tokens still take part in the softmax with score 0 and
+ * add nothing to the output), the rest of the sequence is decoded as usual,
+ * and this bit is set.  The reference indexes the cache tensor with the id
+ * and raises an index error (or reads another page for a negative id). */
+#define KIMI_DEVICE_BAD_PAGE        0x200
 
 enum {
   KIMI_OK = 0,
@@ -106,24 +133,32 @@ typedef struct KimiMlaDecodeParams {
   int32_t num_kv_splits;      /* 1..64 equal splits per sequence, or 0 = balanced schedule (below) */
   float sm_scale;
   float logit_cap;            /* must be 0 (no logit soft-capping on this path) */
+  int32_t* status;            /* optional device word (4-byte aligned): KIMI_DEVICE_* bits are ORed
+                                 into it; never cleared by the library.  NULL = not reported. */
+  uint64_t timeout_ns;        /* bound of each device-side wait in nanoseconds; 0 = 2 s */
 } KimiMlaDecodeParams;
 
 /* Bytes of caller-owned workspace one kimi_mla_decode call needs (split-K
- * partial outputs and log-sum-exps).  num_kv_splits as in the params.
- * Returns 0 for invalid sizes.
+ * partial outputs and log-sum-exps, and the quantised Q operands).
+ * num_kv_splits as in the params.  Returns 0 for invalid sizes.
  *
+ * The decode runs on pairs of CTAs (a thread-block cluster of two SMs: one
+ * computes Q K^T and the softmax, the other P V), one pair per split and
+ * 64-head block.
  * num_kv_splits = S > 0 cuts every sequence into S equal ranges of 128-token
  * tiles, as the reference's num_kv_splits does (S = 1 needs no workspace).
  * num_kv_splits = 0 selects the balanced schedule: the batch's tiles are laid
- * end to end and split evenly over one CTA per SM per 64-head block, so ragged
- * batches and batches smaller than the SM count keep every SM busy; sequences
- * that one CTA covers are written directly, the others merged.  Its workspace
- * is (batch + CTAs) x heads x 1028 bytes plus 8 bytes per sequence, rounded
- * (partials are bf16, log-sum-exps fp32). */
+ * end to end and split evenly over one pair per two SMs per 64-head block, so
+ * ragged batches and batches smaller than the SM count keep every SM busy;
+ * sequences that one pair covers are written directly, the others merged.
+ * The workspace holds slots x heads x 1028 bytes of partials (bf16 rows and
+ * fp32 log-sum-exps; slots = batch x S, or batch + pairs when balanced), 8
+ * bytes per sequence when balanced, and 61440 bytes of Q operands per
+ * sequence and 64-head block, each part rounded up to 256 bytes. */
 KIMI_API size_t kimi_mla_decode_workspace_size(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
 
 /* S for num_kv_splits = S > 0 (capped at 64); for 0, the balanced schedule's
- * CTAs per 64-head block on the current device. */
+ * CTA pairs per 64-head block on the current device. */
 KIMI_API int32_t kimi_mla_decode_num_splits(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
 
 /* Absorbed-MLA decode, one query token per sequence, one KV head. */
@@ -304,6 +339,13 @@ KIMI_API int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* params, void* stream
  * [rows, cols/32], both contiguous. */
 KIMI_API int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride,
                         void* nibbles, void* scales, int32_t legacy_rule, void* stream);
+
+/* Reads a device status word written by the decode kernels (copies 4 bytes
+ * to the host after the work queued on `stream` so far, so it waits for that
+ * work) and returns it: 0 when no bit is set, else the KIMI_DEVICE_* bits (a
+ * positive status below KIMI_ERR_CUDA_BASE), or a CUDA error status.  When
+ * `clear` is non-zero the word is reset to 0 afterwards. */
+KIMI_API int kimi_device_status(int32_t* device_word, int32_t clear, void* stream);
 
 /* Human-readable text for a status code (static storage). */
 KIMI_API const char* kimi_status_string(int status);

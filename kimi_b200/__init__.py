@@ -13,6 +13,8 @@ from .mla import (  # noqa: F401
     TOKEN_BYTES,
     alloc_mxfp4_cache,
     alloc_workspace,
+    check_device_status,
+    device_status,
     mla_decode_fwd,
     mla_decode_merge,
     mla_decode_partial,
@@ -27,7 +29,7 @@ from .mla import (  # noqa: F401
 
 __all__ = [
     "KV_LORA_RANK", "PAGE_SIZE", "QK_DIM", "ROPE_DIM", "SCALE_BYTES", "TOKEN_BYTES",
-    "alloc_mxfp4_cache", "alloc_workspace", "mla_decode_fwd", "mla_decode_merge", "mla_decode_partial",
+    "alloc_mxfp4_cache", "alloc_workspace", "check_device_status", "device_status", "mla_decode_fwd", "mla_decode_merge", "mla_decode_partial",
     "mla_reduce", "mxfp4_kv_append",
     "mxfp4_quantize", "num_kv_splits_for", "q_absorb_rope_append", "v_up_proj_and_o_proj",
     "workspace_bytes",

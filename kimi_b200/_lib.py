@@ -31,7 +31,14 @@ EXPORTED_SYMBOLS = (
     "kimi_mla_q_absorb_rope_append",
     "kimi_ar_rmsnorm_mxfp4",
     "kimi_mla_v_up_o_proj",
+    "kimi_device_status",
 )
+
+ABI_VERSION = 200
+
+# Bits of the decode's device status word (KIMI_DEVICE_* in include/kimi_mla.h).
+DEVICE_WAIT_BITS = 0x1FF
+DEVICE_BAD_PAGE = 0x200
 
 AR_MAX_INPUTS = 8
 
@@ -55,6 +62,8 @@ class KimiMlaDecodeParams(ctypes.Structure):
         ("num_kv_splits", ctypes.c_int32),
         ("sm_scale", ctypes.c_float),
         ("logit_cap", ctypes.c_float),
+        ("status", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_uint64),
     ]
 
 
@@ -193,6 +202,8 @@ def load() -> ctypes.CDLL:
         lib.kimi_ar_rmsnorm_mxfp4.argtypes = [ctypes.POINTER(KimiArRmsNormParams), vp]
         lib.kimi_mla_v_up_o_proj.restype = ctypes.c_int
         lib.kimi_mla_v_up_o_proj.argtypes = [ctypes.POINTER(KimiVUpOProjParams), vp]
+        lib.kimi_device_status.restype = ctypes.c_int
+        lib.kimi_device_status.argtypes = [vp, i32, vp]
         lib.kimi_mxfp4_quantize.restype = ctypes.c_int
         lib.kimi_mxfp4_quantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, vp]
         _lib = lib

@@ -16,6 +16,14 @@ namespace {
 
 using kimi::kLatent;
 
+static_assert(kimi::kStatusSoftmaxWait == KIMI_DEVICE_SOFTMAX_WAIT && kimi::kStatusSoftmaxPvWait == KIMI_DEVICE_SOFTMAX_PV_WAIT &&
+                  kimi::kStatusEpilogueWait == KIMI_DEVICE_EPILOGUE_WAIT && kimi::kStatusIssuerWait == KIMI_DEVICE_ISSUER_WAIT &&
+                  kimi::kStatusIssuerPvWait == KIMI_DEVICE_ISSUER_PV_WAIT &&
+                  kimi::kStatusConverterWait == KIMI_DEVICE_CONVERTER_WAIT && kimi::kStatusDrain == KIMI_DEVICE_DRAIN_WAIT &&
+                  kimi::kStatusProducerWait == KIMI_DEVICE_PRODUCER_WAIT && kimi::kStatusBadPage == KIMI_DEVICE_BAD_PAGE &&
+                  kimi::kStatusScaleWait == KIMI_DEVICE_SCALE_WAIT,
+              "device status bits of the kernels and the header agree");
+
 inline bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 
 inline int cuda_status(cudaError_t e) {
@@ -33,22 +41,6 @@ int device_sm_count() {
   }
   return cached[dev];
 }
-
-// Stage-1 kernel: the block-scaled fp4 tensor-core kernel by default;
-// KIMI_MLA_DECODE_KERNEL=tc selects the fp8-dequantising tcgen05 kernel and
-// =mma the warp-level mma.sync kernel (both kept for comparison).
-enum class Stage1 { kFp4, kTc, kMma };
-
-Stage1 stage1_kernel() {
-  static int choice = -1;
-  if (choice < 0) {
-    const char* v = std::getenv("KIMI_MLA_DECODE_KERNEL");
-    choice = (v && std::strcmp(v, "mma") == 0) ? 2 : (v && std::strcmp(v, "tc") == 0) ? 1 : 0;
-  }
-  return choice == 2 ? Stage1::kMma : choice == 1 ? Stage1::kTc : Stage1::kFp4;
-}
-
-bool use_warp_mma_kernel() { return stage1_kernel() == Stage1::kMma; }
 
 // cuTensorMapEncodeTiled, from the driver through the runtime (no link
 // against libcuda).
@@ -135,38 +127,29 @@ bool encode_bf16_map(CUtensorMap& m, const void* base, cuuint32_t rank, const cu
 // How one call is laid out on the GPU.
 //  * requested splits S > 0: split mode, every sequence cut into S equal tile
 //    ranges (the reference's num_kv_splits), S = 1 writing the output directly;
-//  * requested 0 (auto): balanced mode, one CTA per SM per 64-head block over
-//    the batch's tiles laid end to end (see DecodeArgs in kernels.cuh).  The
-//    mma.sync comparison kernel only has split mode; its auto choice is about
-//    one CTA per SM over (sequence, split, head block), at most 32 splits.
+//  * requested 0 (auto): balanced mode, one pair of CTAs (two SMs) per
+//    64-head block and run over the batch's tiles laid end to end (see
+//    DecodeArgs in kernels.cuh).
 struct Plan {
   bool balanced;
   int ctas;  // balanced: CTAs per head block; split mode: splits per sequence
 };
 
-Plan resolve_plan(int32_t batch, int32_t num_heads, int32_t requested) {
+Plan resolve_plan(int32_t /*batch*/, int32_t num_heads, int32_t requested) {
   const int head_blocks = (num_heads + 63) / 64;
   if (requested > 0) return {false, requested > KIMI_MLA_MAX_SPLITS ? KIMI_MLA_MAX_SPLITS : requested};
-  if (!use_warp_mma_kernel()) {
-    const int c = device_sm_count() / head_blocks;
-    return {true, c < 1 ? 1 : c};
-  }
-  const long ctas = static_cast<long>(batch) * head_blocks;
-  if (ctas <= 0) return {false, 1};
-  long s = (device_sm_count() + ctas / 2) / ctas;
-  if (s < 1) s = 1;
-  if (s > 32) s = 32;
-  return {false, static_cast<int>(s)};
+  const int c = device_sm_count() / 2 / head_blocks;  // one pair of CTAs (two SMs) per run
+  return {true, c < 1 ? 1 : c};
 }
 
 inline size_t round256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
 // Workspace: partial outputs [slots, heads, 512] bf16 (each normalised by its own
 // softmax sum, so bf16 costs one rounding like the output's), log-sum-exps [slots,
-// heads] fp32, then (balanced mode) [batch] int2 CTA spans, then (fp4 kernel)
-// the Q operand images [batch][head blocks] of kQImageBytes.  Split mode has
-// batch * S slots (none for S = 1, and no workspace at all: the fp4 kernel
-// then quantises Q itself), balanced mode batch + ctas.
+// heads] fp32, then (balanced mode) [batch] int2 CTA spans, then the Q
+// operand images [batch][head blocks] of kQImageBytes.  Split mode has
+// batch * S slots (none for S = 1, and no workspace at all: the decode kernel
+// then quantises Q itself, one piece per CTA), balanced mode batch + ctas.
 struct Layout {
   size_t slots, po_bytes, lse_bytes, meta_bytes, qimg_bytes;
   size_t total() const { return po_bytes + lse_bytes + meta_bytes + qimg_bytes; }
@@ -179,8 +162,7 @@ Layout workspace_layout(int64_t batch, int64_t heads, const Plan& plan) {
   l.po_bytes = round256(l.slots * heads * kLatent * sizeof(__nv_bfloat16));
   l.lse_bytes = round256(l.slots * heads * sizeof(float));
   l.meta_bytes = plan.balanced ? round256(static_cast<size_t>(batch) * 2 * sizeof(int32_t)) : 0;
-  if (stage1_kernel() == Stage1::kFp4)
-    l.qimg_bytes = round256(static_cast<size_t>(batch) * ((heads + 63) / 64) * kimi::kQImageBytes);
+  l.qimg_bytes = round256(static_cast<size_t>(batch) * ((heads + 63) / 64) * kimi::kQImageBytes);
   return l;
 }
 
@@ -188,7 +170,7 @@ Layout workspace_layout(int64_t batch, int64_t heads, const Plan& plan) {
 
 extern "C" {
 
-int kimi_abi_version(void) { return 100; }
+int kimi_abi_version(void) { return KIMI_ABI_VERSION; }
 
 const char* kimi_status_string(int status) {
   switch (status) {
@@ -202,6 +184,12 @@ const char* kimi_status_string(int status) {
     case KIMI_ERR_STATIC_WORKSPACE_LIMIT:
       return "split-K partials exceed the library's 32 MiB static workspace (use kimi_mla_decode with a caller workspace)";
     default: break;
+  }
+  if (status > 0 && status < KIMI_ERR_CUDA_BASE) {
+    if (status & KIMI_DEVICE_BAD_PAGE)
+      return (status & ~KIMI_DEVICE_BAD_PAGE) ? "a device wait gave up; a page id was outside the cache"
+                                              : "a page id was outside the cache (its tokens were read as zeros)";
+    return "a device wait gave up (the call's output is not valid)";
   }
   if (status >= KIMI_ERR_CUDA_BASE) return cudaGetErrorString(static_cast<cudaError_t>(status - KIMI_ERR_CUDA_BASE));
   return "unknown status";
@@ -225,7 +213,7 @@ namespace {
 struct Prepared {
   Plan plan;
   kimi::DecodeArgs args;
-  kimi::CacheMaps maps;  // fp4 kernel only
+  kimi::CacheMaps maps;
 };
 
 int prepare(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_bytes, Prepared& out) {
@@ -240,7 +228,8 @@ int prepare(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_byte
     return KIMI_ERR_NULL_POINTER;
   if (p->q_stride_b % 8 || p->q_stride_h % 8 || p->o_stride_b % 4 || p->o_stride_h % 4)
     return KIMI_ERR_BAD_STRIDE;
-  if (!aligned(p->q, 16) || !aligned(p->kv_buffer, 16) || !aligned(p->kv_scales, 16) || !aligned(p->o, 8))
+  if (!aligned(p->q, 16) || !aligned(p->kv_buffer, 16) || !aligned(p->kv_scales, 16) || !aligned(p->o, 8) ||
+      !aligned(p->status, 4))
     return KIMI_ERR_MISALIGNED;
   const Plan plan = resolve_plan(p->batch, p->num_heads, p->num_kv_splits);
   const Layout lay = workspace_layout(p->batch, p->num_heads, plan);
@@ -272,30 +261,24 @@ int prepare(const KimiMlaDecodeParams* p, void* workspace, size_t workspace_byte
   a.num_splits = plan.ctas;
   a.balanced = plan.balanced ? 1 : 0;
   a.sm_scale = p->sm_scale;
-  a.status = nullptr;
-  if (stage1_kernel() == Stage1::kFp4 &&
-      !encode_cache_maps(p->kv_buffer, p->kv_scales, p->num_pages, out.maps.kv, out.maps.sc))
+  a.status = p->status;
+  a.timeout_ns = p->timeout_ns ? p->timeout_ns : kimi::kDefaultTimeoutNs;
+  if (!encode_cache_maps(p->kv_buffer, p->kv_scales, p->num_pages, out.maps.kv, out.maps.sc))
     return KIMI_ERR_UNSUPPORTED;
   out.plan = plan;
   return KIMI_OK;
 }
 
 int launch_stage1(const Prepared& pr, cudaStream_t s) {
-  switch (stage1_kernel()) {
-    case Stage1::kMma: return cuda_status(kimi::launch_decode_mma(pr.args, s));
-    case Stage1::kTc: return cuda_status(kimi::launch_decode_tc(pr.args, s));
-    default: {
-      if (pr.args.q_img) {
-        const int st = cuda_status(kimi::launch_q_prep_fp4(pr.args, s));
-        if (st != KIMI_OK) return st;
-      }
-      return cuda_status(kimi::launch_decode_fp4(pr.args, pr.maps, s));
-    }
+  if (pr.args.q_img) {
+    const int st = cuda_status(kimi::launch_q_prep_fp4(pr.args, s));
+    if (st != KIMI_OK) return st;
   }
+  return cuda_status(kimi::launch_decode_fp4(pr.args, pr.maps, s));
 }
 
 // `after_stage1`: launched right after this call's stage-1 kernel on the same
-// stream; the fp4 kernel lets it start as its programmatic dependent.
+// stream, which lets it start as its programmatic dependent.
 int launch_merge(const Prepared& pr, cudaStream_t s, bool after_stage1) {
   if (!pr.plan.balanced && pr.plan.ctas == 1) return KIMI_OK;  // stage 1 wrote the output
   const kimi::DecodeArgs& a = pr.args;
@@ -311,7 +294,7 @@ int launch_merge(const Prepared& pr, cudaStream_t s, bool after_stage1) {
   r.num_splits = pr.plan.ctas;
   r.seq_meta = a.seq_meta;
   r.kv_indptr = a.kv_indptr;
-  r.programmatic = after_stage1 && stage1_kernel() == Stage1::kFp4 ? 1 : 0;
+  r.programmatic = after_stage1 ? 1 : 0;
   return cuda_status(kimi::launch_reduce(r, s));
 }
 
@@ -523,6 +506,18 @@ int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* p, void* stream) {
     if (!encode_bf16_map(maps.w_o, p->w_o, 2, dims, strides, box)) return KIMI_ERR_UNSUPPORTED;
   }
   return cuda_status(kimi::launch_v_up_o_proj(a, maps, static_cast<cudaStream_t>(stream)));
+}
+
+int kimi_device_status(int32_t* device_word, int32_t clear, void* stream) {
+  if (!device_word) return KIMI_ERR_NULL_POINTER;
+  if (!aligned(device_word, 4)) return KIMI_ERR_MISALIGNED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, device_word, sizeof(host), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(device_word, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_status(e);
+  return host & 0x3FF;
 }
 
 int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,

@@ -232,10 +232,10 @@ struct SchedScratch {
   int scan_warp[32];
 };
 
-// Balanced mode: locate this CTA's run with a block-wide scan of the tiles per
-// sequence (all threads of the CTA call this).
+// Balanced mode: locate run `c` of `ctas` runs with a block-wide scan of the
+// tiles per sequence (all threads of the CTA call this).
 template <int kThreads>
-__device__ void balanced_schedule(const DecodeArgs& a, SchedScratch& ms, Sched& s) {
+__device__ void balanced_schedule(const DecodeArgs& a, SchedScratch& ms, Sched& s, int ctas, int c) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
     ms.tmin = 0x7fffffff;
@@ -272,7 +272,6 @@ __device__ void balanced_schedule(const DecodeArgs& a, SchedScratch& ms, Sched& 
     total += v;
   }
   const int excl = before + incl - mine;
-  const int ctas = gridDim.x, c = blockIdx.x;
   long long start = static_cast<long long>(c) * total / ctas;
   long long end = static_cast<long long>(c + 1) * total / ctas;
   const int seq_t = ms.tmax;

@@ -70,6 +70,13 @@ __global__ void __launch_bounds__(256) mla_reduce_kernel(ReduceArgs a) {
       return;
     }
     const int2 span = a.seq_meta[b];
+    if (span.x < 0 || span.y < span.x || span.y >= a.num_splits) {
+      // Not a span the decode wrote (it gave up before recording it; its
+      // status word says so): zeros, and no read outside the workspace.
+#pragma unroll
+      for (int k = 0; k < 4; ++k) reinterpret_cast<uint2*>(out)[k] = make_uint2(0u, 0u);
+      return;
+    }
     if (span.x == span.y) return;  // written by the decode kernel itself
     first_slot = static_cast<int64_t>(b) + span.x;
     n_slots = span.y - span.x + 1;

@@ -21,12 +21,14 @@
 //    them.  Nothing in it needs clearing between calls: each call writes
 //    every log-sum-exp slot and every partial row that its merge reads.
 //  * The device address of the array is looked up with cudaGetSymbolAddress
-//    on the first call on each device (with that device current); make that
-//    first call before any stream capture begins.
+//    on the first call on each device (with that device current), and again
+//    on the first call after that device's context changed (a
+//    cudaDeviceReset); make those calls before any stream capture begins.
 #include <cstddef>
 #include <cstdint>
 #include <mutex>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/kimi_mla.h"
@@ -42,22 +44,58 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticWorkspaceBytes];
 
 std::mutex g_mutex;
-void* g_device_ptr[kMaxDevices] = {nullptr};
 
-// Device address of g_decode_scratch on the current device (looked up once).
+// The address is valid for the device's primary context that was current
+// when it was looked up; a later context on the same device (after
+// cudaDeviceReset, say) gets its own lookup.  The current context comes from
+// the driver through the runtime (no link against libcuda).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  return fn;
+}
+
+struct Entry {
+  CUcontext ctx = nullptr;
+  void* ptr = nullptr;
+};
+Entry g_entry[kMaxDevices];
+
+// Device address of g_decode_scratch on the current device and context.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return KIMI_ERR_CUDA_BASE + static_cast<int>(e);
   if (dev < 0 || dev >= kMaxDevices) return KIMI_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_device_ptr[dev]) {
+  const CtxGetCurrentFn get = ctx_get_current();
+  auto current = [get]() {
+    CUcontext c = nullptr;
+    if (get && get(&c) != CUDA_SUCCESS) c = nullptr;
+    return c;
+  };
+  // (no context is current before the runtime first touches the device:
+  // the lookup below creates it, and the context is read again after it)
+  CUcontext ctx = current();
+  Entry& en = g_entry[dev];
+  if (!en.ptr || !ctx || en.ctx != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_decode_scratch);
     if (e != cudaSuccess) return KIMI_ERR_CUDA_BASE + static_cast<int>(e);
-    g_device_ptr[dev] = p;
+    en.ptr = p;
+    en.ctx = current();
   }
-  *out = g_device_ptr[dev];
+  *out = en.ptr;
   return KIMI_OK;
 }
 

@@ -106,9 +106,12 @@ def _default_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
 
 
 def _run_decode(entry: str, q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
-                max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits, workspace):
+                max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits, workspace,
+                status=None, timeout_ns=0):
     """Checks the arguments, fills the C-ABI params and calls ``entry``."""
     dev = _require_cuda(q, kv_buffer, kv_scales, o, kv_indptr, kv_indices)
+    if status is not None:
+        _require_status_word(status, dev)
     if max_seqlen_q != 1:
         raise ValueError("mla_decode_fwd supports one query token per sequence (max_seqlen_q == 1)")
     if page_size != PAGE_SIZE:
@@ -148,7 +151,7 @@ def _run_decode(entry: str, q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv
         kv_last_page_len=_ptr(kv_last_page_len),
         o=o.data_ptr(), o_stride_b=o.stride(0), o_stride_h=o.stride(1),
         batch=batch, num_heads=heads, num_kv_splits=splits_req,
-        sm_scale=scale, logit_cap=float(logit_cap))
+        sm_scale=scale, logit_cap=float(logit_cap), status=_ptr(status), timeout_ns=int(timeout_ns))
     if p.kv_indices is None and batch:
         # an all-empty batch still needs a valid pointer; the kernel never reads past kv_indptr
         p.kv_indices = kv_indptr.data_ptr()
@@ -164,7 +167,8 @@ def mla_decode_fwd(q: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Te
                    qo_indptr: torch.Tensor | None, kv_indptr: torch.Tensor, kv_indices: torch.Tensor,
                    kv_last_page_len: torch.Tensor | None, max_seqlen_q: int = 1, page_size: int = PAGE_SIZE,
                    nhead_kv: int = 1, sm_scale: float | None = None, logit_cap: float = 0.0,
-                   num_kv_splits: int | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+                   num_kv_splits: int | None = None, workspace: torch.Tensor | None = None,
+                   status: torch.Tensor | None = None, timeout_ns: int = 0) -> torch.Tensor:
     """Absorbed-MLA decode over the paged MXFP4 latent cache; writes ``o``.
 
     q            bf16 [batch, num_heads, 576] (rows may be strided; last dim contiguous)
@@ -177,22 +181,27 @@ def mla_decode_fwd(q: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Te
     num_kv_splits equal split-K ranges per sequence (the reference's meaning),
                  or None / 0 for the balanced schedule over all SMs;
                  workspace optional uint8 buffer of at least :func:`workspace_bytes`
+    status       optional int32 [1] device word: the kernels OR KIMI_DEVICE_* bits
+                 into it when a bounded device wait gives up or a page id lies
+                 outside the cache (read it with :func:`device_status`)
+    timeout_ns   bound of each device-side wait (0 = the library default, 2 s)
     """
     return _run_decode("kimi_mla_decode", q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices,
                        kv_last_page_len, max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits,
-                       workspace)
+                       workspace, status, timeout_ns)
 
 
 def mla_decode_partial(q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
                        max_seqlen_q: int = 1, page_size: int = PAGE_SIZE, nhead_kv: int = 1,
                        sm_scale: float | None = None, logit_cap: float = 0.0, num_kv_splits: int | None = None,
-                       workspace: torch.Tensor | None = None) -> torch.Tensor:
+                       workspace: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                       timeout_ns: int = 0) -> torch.Tensor:
     """The split-K attention launch of :func:`mla_decode_fwd` alone (the
     archive's ``_mla_decode_split_kv``); pair it with :func:`mla_decode_merge`
     on the same arguments and workspace."""
     return _run_decode("kimi_mla_decode_partial", q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices,
                        kv_last_page_len, max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits,
-                       workspace)
+                       workspace, status, timeout_ns)
 
 
 def mla_decode_merge(q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
@@ -204,6 +213,32 @@ def mla_decode_merge(q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indice
     return _run_decode("kimi_mla_decode_merge", q, kv_buffer, kv_scales, o, qo_indptr, kv_indptr, kv_indices,
                        kv_last_page_len, max_seqlen_q, page_size, nhead_kv, sm_scale, logit_cap, num_kv_splits,
                        workspace)
+
+
+def _require_status_word(status: torch.Tensor, dev: torch.device) -> None:
+    if status.dtype != torch.int32 or status.numel() != 1 or status.device != dev:
+        raise ValueError(f"status must be an int32 tensor of one element on {dev}")
+
+
+def device_status(status: torch.Tensor, clear: bool = False) -> int:
+    """The KIMI_DEVICE_* bits in a decode status word (0 = none), read after
+    the work queued on the current stream (this waits for it).  ``clear``
+    resets the word afterwards."""
+    dev = _require_cuda(status)
+    _require_status_word(status, dev)
+    with torch.cuda.device(dev):
+        st = _lib.load().kimi_device_status(status.data_ptr(), int(bool(clear)), _stream_handle(dev))
+    if st >= _lib.KIMI_ERR_CUDA_BASE or st < 0:
+        _lib.check(st, "kimi_device_status")
+    return int(st)
+
+
+def check_device_status(status: torch.Tensor, clear: bool = False) -> None:
+    """Raise ``RuntimeError`` when a decode recorded a device-side failure in
+    ``status`` (a wait that gave up, or a page id outside the cache)."""
+    st = device_status(status, clear)
+    if st:
+        raise RuntimeError(f"MLA decode reported a device-side failure: {_lib.status_text(st)} (bits {st:#x})")
 
 
 def mla_reduce(partial_o: torch.Tensor, partial_lse: torch.Tensor, o: torch.Tensor) -> torch.Tensor:

@@ -115,7 +115,8 @@ class CudaIpc:
 
     def close(self, base: int):
         from cuda.bindings import runtime
-        runtime.cudaIpcCloseMemHandle(base)
+        err, = runtime.cudaIpcCloseMemHandle(base)
+        _check_cuda(err, "cudaIpcCloseMemHandle")
 
     def synchronize(self, device: torch.device):
         torch.cuda.synchronize(device)
@@ -147,14 +148,26 @@ class PeerPartials:
         self.rows, self.hidden = rows, hidden
         self.local = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=self.device)
         ptr = self.local.data_ptr()
+        # Every rank joins the gather even when its export failed (an
+        # allocation from PYTORCH_CUDA_ALLOC_CONF=expandable_segments has no
+        # IPC handle, for one): each sends (ok, payload) and all of them raise
+        # together, instead of the peers waiting out the group's timeout.
+        try:
+            mine = (True, self.ipc.export(ptr))
+        except Exception as e:  # noqa: BLE001 - reported to every rank below
+            mine = (False, f"{type(e).__name__}: {e}")
         shared = [None] * self.world
-        dist.all_gather_object(shared, self.ipc.export(ptr), group=group)
+        dist.all_gather_object(shared, mine, group=group)
+        failed = [(r, msg) for r, (ok, msg) in enumerate(shared) if not ok]
+        if failed:
+            raise RuntimeError("PeerPartials: IPC export failed on rank(s) " +
+                               "; ".join(f"{r}: {msg}" for r, msg in failed))
         # open every peer's allocation with this rank's GPU current: the mapping
         # (and the peer access it enables) belongs to this GPU's context
         self.ipc.make_current(self.device)
         self._opened, self.ptrs = [], []
         try:
-            for r, (raw, offset) in enumerate(shared):
+            for r, (_, (raw, offset)) in enumerate(shared):
                 if r == self.rank:
                     self.ptrs.append(ptr)
                     continue
@@ -162,19 +175,35 @@ class PeerPartials:
                 self._opened.append(base)
                 self.ptrs.append(base + offset)
         except Exception:
-            for b in self._opened:
-                self.ipc.close(b)
-            self._opened, self.ptrs = [], []
+            self._unmap()
             raise
+
+    def _unmap(self):
+        """Close every mapping this rank opened; the first failure is raised
+        once all of them have been tried."""
+        first = None
+        for b in self._opened:
+            try:
+                self.ipc.close(b)
+            except Exception as e:  # noqa: BLE001 - re-raised below
+                first = first or e
+        self._opened, self.ptrs = [], []
+        if first is not None:
+            raise first
 
     def close(self):
         """Unmap the peers' buffers (collective: call on every rank once no
-        kernel reads them any more)."""
+        kernel reads them any more).  Every rank reaches the closing barrier
+        even when an unmap failed; the failure is raised after it."""
         self.ipc.synchronize(self.device)
-        for b in self._opened:
-            self.ipc.close(b)
-        self._opened, self.ptrs = [], []
+        err = None
+        try:
+            self._unmap()
+        except Exception as e:  # noqa: BLE001 - re-raised after the barrier
+            err = e
         self._barrier()
+        if err is not None:
+            raise err
 
     def _barrier(self):
         import torch.distributed as dist

@@ -29,21 +29,41 @@ def test_library_exports_every_declared_symbol():
 
 def test_status_strings_and_version():
     lib = _lib.load()
-    assert lib.kimi_abi_version() == 100
+    assert lib.kimi_abi_version() == _lib.ABI_VERSION == 200
     assert _lib.status_text(0) == "ok"
     assert "workspace" in _lib.status_text(-5)
     assert _lib.status_text(-12345) == "unknown status"
 
 
-# Q operand images of the fp4 kernel per (sequence, 64-head block): three e2m1
-# terms (2 x 192 x 128 B), q_pe (64 x 128 B) and the terms' scales (192 x 16 B)
-Q_IMAGE_BYTES = 2 * 192 * 128 + 64 * 128 + 192 * 16
+def test_device_status_texts():
+    # positive codes below KIMI_ERR_CUDA_BASE are device status words
+    # (KIMI_DEVICE_* bits) read back by kimi_device_status
+    assert "gave up" in _lib.status_text(0x010)
+    assert "gave up" in _lib.status_text(0x001 | 0x080)
+    bad = _lib.status_text(_lib.DEVICE_BAD_PAGE)
+    assert "outside the cache" in bad and "gave up" not in bad
+    both = _lib.status_text(_lib.DEVICE_BAD_PAGE | 0x040)
+    assert "gave up" in both and "outside the cache" in both
+    # CUDA errors keep their own range
+    assert "gave up" not in _lib.status_text(_lib.KIMI_ERR_CUDA_BASE + 2)
+
+
+def test_device_status_argument_checks():
+    lib = _lib.load()
+    assert lib.kimi_device_status(None, 0, None) == -1  # KIMI_ERR_NULL_POINTER
+    assert lib.kimi_device_status(3, 0, None) == -4  # KIMI_ERR_MISALIGNED
+
+
+# Q operand images of the decode kernel per (sequence, 64-head block): three
+# e2m1 terms (2 x 192 x 128 B), q_pe (64 x 128 B) and the terms' scales in the
+# tcgen05.cp order (8 blocks of 512 B)
+Q_IMAGE_BYTES = 2 * 192 * 128 + 64 * 128 + 8 * 512
 
 
 def test_workspace_size_arithmetic():
     lib = _lib.load()
     # explicit splits: partial O (B*S*H*512 bf16) + LSE (B*S*H f32) + the fp4
-    # kernel's Q operand images (B * head blocks * 60416 B), each rounded to 256 B
+    # kernel's Q operand images (B * head blocks * 61440 B), each rounded to 256 B
     b, h, s = 64, 64, 4
     rows = b * s * h
     r256 = lambda n: ((n + 255) // 256) * 256
@@ -88,6 +108,9 @@ def test_decode_rejects_bad_arguments_on_host():
     p.q_stride_h = 577
     assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -3
     p.q_stride_h = 576
+    p.status = 0x6002  # the optional device status word must be 4-byte aligned
+    assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -4
+    p.status = None
     p.num_kv_splits = 4
     assert lib.kimi_mla_decode(ctypes.byref(p), None, 0, None) == -5  # no workspace for 4 splits
     # batch 0 is a no-op

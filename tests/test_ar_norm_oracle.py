@@ -34,3 +34,20 @@ def test_single_input_is_residual_add_and_norm():
     comb, _, _, _ = ar_norm.ar_rmsnorm_mxfp4([x], res, w, 1e-6)
     want = omx.f32_to_bf16_bits((omx.bf16_bits_to_f32(x) + omx.bf16_bits_to_f32(res)).astype(np.float32))
     np.testing.assert_array_equal(comb, want)
+
+
+def test_oracle_matches_reference_rmsnorm_lines_golden():
+    """rmsnorm_golden.npz holds the output of the reference's own statements
+    (tests/test_ar_fusion_correctness.py:128-131, run by
+    tests/golden/make_rmsnorm_golden.py on CPU torch): the new residual and
+    the normed, weighted rows are bit-exact, for 1 and 4 rows of 7168."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "rmsnorm_golden.npz"))
+    for n in ("m1", "m4"):
+        comb, out, nib, sc = ar_norm.ar_rmsnorm_mxfp4([g[f"{n}_hidden_states"]], g[f"{n}_residual"],
+                                                      g[f"{n}_weight"], float(g["eps"]))
+        np.testing.assert_array_equal(comb, g[f"{n}_combined"])
+        np.testing.assert_array_equal(out, g[f"{n}_normed_output"])
+        n2, s2 = omx.quantize_inline(g[f"{n}_normed_output"])
+        np.testing.assert_array_equal(nib, n2)
+        np.testing.assert_array_equal(sc, s2)

@@ -49,6 +49,22 @@ def test_matches_oracle(n, rows, hidden, legacy):
     np.testing.assert_array_equal(g_sc.cpu().numpy(), sc)
 
 
+def test_matches_reference_rmsnorm_lines_golden():
+    """The kernel on the inputs of rmsnorm_golden.npz (one rank: the
+    all-reduce is the identity) against the reference's own statements
+    (tests/test_ar_fusion_correctness.py:128-131): the new residual bit-exact,
+    the nibbles and scales those of MXFP4 of the reference's normed rows."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "rmsnorm_golden.npz"))
+    for n in ("m1", "m4"):
+        r_out, g_nib, g_sc = tp.ar_rmsnorm_mxfp4([_t(g[f"{n}_hidden_states"])], _t(g[f"{n}_residual"]),
+                                                 _t(g[f"{n}_weight"]), float(g["eps"]))
+        torch.cuda.synchronize()
+        nib, sc = omx.quantize_inline(g[f"{n}_normed_output"])
+        np.testing.assert_array_equal(_bits(r_out), g[f"{n}_combined"])
+        np.testing.assert_array_equal(g_nib.cpu().numpy(), nib)
+        np.testing.assert_array_equal(g_sc.cpu().numpy(), sc)
+
+
 def test_residual_updated_in_place():
     rng = np.random.default_rng(70)
     ins = [_bf16_np(rng, (16, 7168)) for _ in range(2)]

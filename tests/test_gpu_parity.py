@@ -214,7 +214,7 @@ def test_reduce_against_oracle_merge():
 # full-size properties (the Kimi-K2 decode shape)
 # ---------------------------------------------------------------------------
 def test_full_size_kimi_k2_shape_subset_and_split_invariance():
-    """64 heads, batch 64, ctx 8192, random page permutation: a subset of
+    """64 heads, batch 64, ctx 8192, random page permutation: 16 of the 64
     sequences against the oracle, and the auto split count against 1 and 32
     splits."""
     b, h, ctx = 64, 64, 8192
@@ -241,7 +241,7 @@ def test_full_size_kimi_k2_shape_subset_and_split_invariance():
     kvb_np, kvs_np = kvb.cpu().numpy(), kvs.cpu().numpy()
     q_bits = q.cpu().view(torch.int16).numpy().view(np.uint16)
     perm_np = perm.cpu().numpy()
-    for seq in (0, 37, 63):
+    for seq in range(0, 64, 4):  # 16 sequences, a quarter of the batch
         pg = perm_np[seq * 128:(seq + 1) * 128]
         ref = omla.mla_decode(q_bits[seq:seq + 1], kvb_np, kvs_np, np.array([0, 128], np.int32), pg,
                               np.array([64], np.int32), sm)

@@ -93,3 +93,57 @@ def test_two_rank_exchange_and_teardown(tmp_path):
     mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     for r in range(world):
         assert (tmp_path / f"rank{r}").read_text() == "ok"
+
+
+class FailingExportIpc(FakeIpc):
+    """Rank 1's export fails (as cudaIpcGetMemHandle does on an allocation
+    from expandable segments)."""
+
+    def export(self, ptr):
+        if self.rank == 1:
+            raise RuntimeError("cudaIpcGetMemHandle failed: CUDA error 1")
+        return super().export(ptr)
+
+
+class FailingCloseIpc(FakeIpc):
+    """Every unmap reports an error after recording the call."""
+
+    def close(self, base):
+        super().close(base)
+        raise RuntimeError("cudaIpcCloseMemHandle failed: CUDA error 400")
+
+
+def _failure_rank_main(rank, world, port, result_dir):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    # a short group timeout: a rank left waiting in a collective fails the test quickly
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        # one rank's export fails: every rank joins the gather and raises the same error
+        ipc = FailingExportIpc(rank)
+        with pytest.raises(RuntimeError, match=r"export failed on rank\(s\) 1: RuntimeError: cudaIpcGetMemHandle"):
+            tp.PeerPartials(16, 256, torch.device("cpu"), ipc=ipc)
+        assert ipc.opened == []
+        # an unmap error is raised, after the closing barrier every rank reaches
+        ipc = FailingCloseIpc(rank)
+        peers = tp.PeerPartials(16, 256, torch.device("cpu"), ipc=ipc)
+        with pytest.raises(RuntimeError, match="cudaIpcCloseMemHandle"):
+            peers.close()
+        assert sorted(ipc.closed) == sorted(ipc.opened) and peers.ptrs == []
+        # the group is still in step: one more collective completes on both ranks
+        t = torch.ones(1)
+        dist.all_reduce(t)
+        assert t.item() == world
+        with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
+            f.write("ok")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_export_and_unmap_failures_raise_on_every_rank(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.spawn(_failure_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        assert (tmp_path / f"rank{r}").read_text() == "ok"

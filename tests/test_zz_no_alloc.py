@@ -87,6 +87,30 @@ def test_static_workspace_decode_matches_regular_entry_point_twice_in_a_row():
     assert np.array_equal(again, first)
 
 
+def test_static_workspace_balanced_schedule_after_a_call_that_filled_the_array():
+    """The balanced schedule (num_kv_splits = 0) reads partial rows, log-sum-
+    exps and CTA-pair spans from slots that differ from call to call.  A first
+    call in split mode fills several MiB of the array with its own partials;
+    a balanced call after it, on ragged sequences that straddle pairs, must
+    still match the regular entry point: it writes every slot its merge
+    reads, whatever the array held."""
+    lib = _lib.load()
+    fill = make_case([2048] * 16, 64, seed=5)      # 16 x 16 splits x 64 heads of partials
+    ragged = make_case([8192, 300, 5000, 64, 12000, 1, 2048, 700], 64, seed=6)
+    need_fill = lib.kimi_mla_decode_workspace_size(16, 64, 16)
+    need_bal = lib.kimi_mla_decode_workspace_size(8, 64, 0)
+    assert need_bal <= need_fill <= 32 << 20
+    _run_static(lib, fill, 16)
+    got = _run_static(lib, ragged, 0)
+    want = _run_regular(lib, ragged, 0)
+    cos, err = compare(got, want)
+    assert cos >= COS_MIN and err <= MAX_ABS, (cos, err)
+    cos, err = compare(got, oracle_out(ragged))
+    assert cos >= COS_MIN and err <= MAX_ABS, (cos, err)
+    # and twice in a row: the same call again gives the same bits
+    assert np.array_equal(_run_static(lib, ragged, 0), got)
+
+
 def test_static_workspace_rejects_sizes_beyond_its_limit():
     lib = _lib.load()
     # 128 sequences x 64 splits x 128 heads of partials is far beyond 32 MiB

@@ -405,7 +405,7 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded normal q and latents, cache written by the library's MXFP4 KV-append)",
         "config": ({"workload": RAGGED_WORKLOAD, "heads": HEADS, "batch_total": RAGGED_BATCH,
                     "batch_this_rank": wl[0]["batch"], "tokens_total": sum(wl[0]["lens"]), "page_size": PAGE,
-                    "num_kv_splits": f"auto (balanced schedule over {splits} CTA pairs)", "sm_scale": "1/sqrt(192)",
+                    "num_kv_splits": f"auto (balanced schedule over {splits} CTAs)", "sm_scale": "1/sqrt(192)",
                     "algorithmic_bytes_per_job_step": nbytes_job,
                     "l2": "inputs larger than L2: one ~1.7 GB / N cache per rank",
                     "parallelism": f"dp{world} (sequences bin-packed over ranks; outputs gathered to rank 0 "
@@ -413,7 +413,7 @@ def run_ours(args, rank, world, local_rank):
                     "gather_ms": None if gather_ms is None else round(gather_ms, 5)}
                    if ragged else
                    {"workload": WORKLOAD, "heads": HEADS, "batch_per_gpu": BATCH, "ctx": CTX, "page_size": PAGE,
-                    "num_kv_splits": f"auto (balanced schedule over {splits} CTA pairs)", "sm_scale": "1/sqrt(192)",
+                    "num_kv_splits": f"auto (balanced schedule over {splits} CTAs)", "sm_scale": "1/sqrt(192)",
                     "algorithmic_bytes_per_gpu_step": nbytes,
                     "l2": "inputs larger than L2: two independent 210 MB caches alternated between steps",
                     "parallelism": f"dp{world} (batch-sharded, no collective in the step)"}),

@@ -127,9 +127,9 @@ bool encode_bf16_map(CUtensorMap& m, const void* base, cuuint32_t rank, const cu
 // How one call is laid out on the GPU.
 //  * requested splits S > 0: split mode, every sequence cut into S equal tile
 //    ranges (the reference's num_kv_splits), S = 1 writing the output directly;
-//  * requested 0 (auto): balanced mode, one pair of CTAs (two SMs) per
-//    64-head block and run over the batch's tiles laid end to end (see
-//    DecodeArgs in kernels.cuh).
+//  * requested 0 (auto): balanced mode, one CTA per SM and 64-head block,
+//    each a run over the batch's tiles laid end to end (see DecodeArgs in
+//    kernels.cuh).
 struct Plan {
   bool balanced;
   int ctas;  // balanced: CTAs per head block; split mode: splits per sequence
@@ -138,7 +138,7 @@ struct Plan {
 Plan resolve_plan(int32_t /*batch*/, int32_t num_heads, int32_t requested) {
   const int head_blocks = (num_heads + 63) / 64;
   if (requested > 0) return {false, requested > KIMI_MLA_MAX_SPLITS ? KIMI_MLA_MAX_SPLITS : requested};
-  const int c = device_sm_count() / 2 / head_blocks;  // one pair of CTAs (two SMs) per run
+  const int c = device_sm_count() / head_blocks;  // one CTA per SM and head block
   return {true, c < 1 ? 1 : c};
 }
 

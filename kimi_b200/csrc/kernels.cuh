@@ -21,21 +21,11 @@ constexpr int kPageScaleBytes = kPageSize * kScaleBytes;   // 1024
 // Q operands of the fp4 kernel for one (sequence, 64-head block), as the
 // shared-memory images its QK^T MMAs read: three block-scaled e2m1 terms
 // (2 K blocks x 192 rows x 128 B, 128-byte swizzle), q_pe (64 rows x 128 B,
-// same swizzle), then the terms' e8m0 scales in the order tcgen05.cp moves
-// them into TMEM (see q_sf_offset).
+// same swizzle), then the terms' e8m0 scales as [192 rows][16 blocks].
 constexpr int kQTermBytes = 2 * 192 * 128;   // 49152
 constexpr int kQPeBytes = 64 * 128;          // 8192
-constexpr int kQScaleBytes = 8 * 512;        // 4096: 4 scale blocks x 2 row blocks of 512 B
-constexpr int kQImageBytes = kQTermBytes + kQPeBytes + kQScaleBytes;  // 61440
-
-// Byte offset of the e8m0 scale of row n (0..255) and 32-element group g
-// (0..15) of a block-scaled MMA operand, laid out for tcgen05.cp
-// 32x128b.warpx4: a 512-byte block per (scale block g / 4, row block n / 128);
-// inside it row n % 32 owns 16 bytes, word (n % 128) / 32 of which holds the
-// four scales of groups 4 (g / 4) .. 4 (g / 4) + 3.
-__host__ __device__ constexpr int q_sf_offset(int n, int g) {
-  return ((g >> 2) * 2 + (n >> 7)) * 512 + (n & 31) * 16 + ((n >> 5) & 3) * 4 + (g & 3);
-}
+constexpr int kQScaleBytes = 192 * 16;       // 3072
+constexpr int kQImageBytes = kQTermBytes + kQPeBytes + kQScaleBytes;  // 60416
 
 // Bits of the decode's device status word (DecodeArgs::status): which wait
 // gave up, or a page id outside the cache.
@@ -150,21 +140,18 @@ struct QuantizeArgs {
   int legacy_rule;
 };
 
-// Split-K decode.  Stage 1 runs on pairs of CTAs (clusters of two: the QK
-// CTA and the PV CTA) and covers each sequence's 128-token tiles with one or
+// Split-K decode.  Stage 1 covers each sequence's 128-token tiles with one or
 // more pieces; a piece that holds a whole sequence writes the final bf16
 // output, any other writes a partial output (normalised by its own softmax
 // sum) and its natural-log log-sum-exp to a workspace slot.
-//   * split mode (balanced = 0): grid (2 num_splits, batch, head blocks); pair
-//     s of row b takes the s-th of num_splits equal tile ranges of sequence b,
-//     slot b * num_splits + s; with one split the pair writes the output
-//     directly.
-//   * balanced mode (balanced = 1): grid (2 pairs, 1, head blocks); pair c
-//     takes tiles [c T / pairs, (c + 1) T / pairs) of all T tiles of the batch
-//     laid end to end, slot b + c for its piece of sequence b (unique: along
-//     the tile list both b and c only grow), and the pair holding a
-//     sequence's first tile records (first pair, last pair) of that sequence
-//     in seq_meta for the merge.
+//   * split mode (balanced = 0): grid (num_splits, batch, head blocks); CTA
+//     (s, b) takes the s-th of num_splits equal tile ranges of sequence b, slot
+//     b * num_splits + s; with one split the CTA writes the output directly.
+//   * balanced mode (balanced = 1): grid (ctas, 1, head blocks); CTA c takes
+//     tiles [c T / ctas, (c + 1) T / ctas) of all T tiles of the batch laid end
+//     to end, slot b + c for its piece of sequence b (unique: along the tile
+//     list both b and c only grow), and the CTA holding a sequence's first tile
+//     records (first CTA, last CTA) of that sequence in seq_meta for the merge.
 struct DecodeArgs {
   const __nv_bfloat16* q;
   int64_t q_stride_b;
@@ -181,11 +168,11 @@ struct DecodeArgs {
   __nv_bfloat16* partial_o;  // [slots, heads, 512] bf16 (the merge restores fp32 sums)
   float* partial_lse;  // [batch, splits, heads]
   int* status;         // optional device word: kStatus* bits (a wait that gave up, a bad page id)
-  int2* seq_meta;      // balanced mode: [batch] (first pair, last pair) of each sequence's tiles
+  int2* seq_meta;      // balanced mode: [batch] (first CTA, last CTA) of each sequence's tiles
   const uint8_t* q_img;  // fp4 kernel: [batch][head blocks] Q operand images (kQImageBytes each), or null
   int batch;
   int num_heads;
-  int num_splits;      // split mode: splits per sequence; balanced mode: CTA pairs per head block
+  int num_splits;      // split mode: splits per sequence; balanced mode: CTAs per head block
   int balanced;        // 1: balanced mode
   float sm_scale;
   unsigned long long timeout_ns;  // bound of each device wait (the drain's excepted)
@@ -208,7 +195,7 @@ struct ReduceArgs {
   int64_t o_stride_h;
   int batch;
   int num_heads;
-  int num_splits;             // split mode: slots b * num_splits + s; balanced mode: CTA pairs (spans lie in [0, num_splits))
+  int num_splits;             // split mode: slots b * num_splits + s; balanced mode: CTAs (spans lie in [0, num_splits))
   const int2* seq_meta;       // balanced mode (non-null): slots b + c, c in [meta.x, meta.y]
   const int32_t* kv_indptr;   // balanced mode: sequences without pages get zeros
   int programmatic;           // launched as a programmatic dependent of the decode kernel (waits for it)

@@ -324,35 +324,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Wait for the phase with the given parity to complete for at most
+// Wait for the phase with the given parity to complete for at most about
 // `timeout_ns` nanoseconds of global time (each poll sleeping up to
-// min(kWaitSleepNs, timeout_ns)), giving up early once *abort is non-zero.
-// Returns false on give-up.
+// min(kWaitSleepNs, timeout_ns); the clock is read from the second poll on,
+// so a wait that the first poll ends costs no timer read), giving up early
+// once *abort is non-zero.  Returns false on give-up.
 __device__ __forceinline__ bool mbar_wait_timed(uint64_t* mbar, uint32_t parity, uint64_t timeout_ns,
                                                 const volatile int* abort) {
   const uint32_t hint = timeout_ns < kWaitSleepNs ? static_cast<uint32_t>(timeout_ns) : kWaitSleepNs;
+  if (mbar_try_wait_sleep(mbar, parity, hint)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait_sleep(mbar, parity, hint)) return true;
     if (abort && *abort) return false;
     if (globaltimer_ns() - t0 >= timeout_ns) return false;
   }
-}
-
-// ---------------------------------------------------------------------------
-// Shared memory -> TMEM copy (tcgen05.cp), issued by one thread and ordered
-// with the MMAs that same thread issues after it.
-// ---------------------------------------------------------------------------
-
-// 32 rows x 16 bytes from shared memory (row r at byte 16 r of `sdesc`'s
-// start, described as a K-major no-swizzle operand: 8-row core matrices 128
-// bytes apart) into TMEM lanes 0..31, columns taddr .. taddr + 3 (row r ->
-// lane r, its four 32-bit words -> the four columns), copied identically into
-// all four 32-lane quarters.  This is the layout of the e8m0 scale factors of
-// a block-scaled MMA operand: lane r, column c holds the four scale bytes of
-// row r + 32 c.
-__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -410,101 +396,6 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
   const float lo = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
   const float hi = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 >> 16)));
   return make_float2(lo, hi);
-}
-
-}  // namespace sm100
-}  // namespace kimi
-
-namespace kimi {
-namespace sm100 {
-
-// ---------------------------------------------------------------------------
-// Thread-block clusters (distributed shared memory between the CTAs of a
-// cluster; no TMA multicast)
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-  return r;
-}
-
-// Shared::cluster address of the variable at local shared address `saddr` in
-// the cluster's CTA `rank`.
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void st_cluster_v4(uint32_t caddr, uint4 v) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(caddr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ void st_cluster_f32(uint32_t caddr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(caddr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_cluster_u32(uint32_t caddr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(caddr), "r"(v) : "memory");
-}
-
-// Arrive on an mbarrier of another CTA of the cluster (release at cluster
-// scope: this thread's earlier shared::cluster writes are visible to the
-// thread that observes the phase).
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(caddr) : "memory");
-}
-
-// Probes for phases completed by arrivals from other CTAs (acquire at
-// cluster scope).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* mbar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(mbar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t* mbar, uint32_t parity, uint32_t ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(mbar)), "r"(parity), "r"(ns)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_timed_cluster(uint64_t* mbar, uint32_t parity, uint64_t timeout_ns,
-                                                        const volatile int* abort) {
-  const uint32_t hint = timeout_ns < kWaitSleepNs ? static_cast<uint32_t>(timeout_ns) : kWaitSleepNs;
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-    if (mbar_try_wait_cluster_sleep(mbar, parity, hint)) return true;
-    if (abort && *abort) return false;
-    if (globaltimer_ns() - t0 >= timeout_ns) return false;
-  }
-}
-
-// Every thread of every CTA of the cluster arrives
-// (release) and waits (acquire).
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-
-// Arrive (once) on the mbarrier at the same shared-memory offset in every CTA
-// of `cta_mask` when all earlier tcgen05 operations of this thread complete.
-__device__ __forceinline__ void mma_commit_multicast(uint64_t* mbar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(
-          smem_addr(mbar)),
-      "h"(cta_mask)
-      : "memory");
 }
 
 }  // namespace sm100

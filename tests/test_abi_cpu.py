@@ -55,15 +55,15 @@ def test_device_status_argument_checks():
 
 
 # Q operand images of the decode kernel per (sequence, 64-head block): three
-# e2m1 terms (2 x 192 x 128 B), q_pe (64 x 128 B) and the terms' scales in the
-# tcgen05.cp order (8 blocks of 512 B)
-Q_IMAGE_BYTES = 2 * 192 * 128 + 64 * 128 + 8 * 512
+# e2m1 terms (2 x 192 x 128 B), q_pe (64 x 128 B) and the terms' e8m0 scales
+# (192 rows x 16 blocks)
+Q_IMAGE_BYTES = 2 * 192 * 128 + 64 * 128 + 192 * 16
 
 
 def test_workspace_size_arithmetic():
     lib = _lib.load()
     # explicit splits: partial O (B*S*H*512 bf16) + LSE (B*S*H f32) + the fp4
-    # kernel's Q operand images (B * head blocks * 61440 B), each rounded to 256 B
+    # kernel's Q operand images (B * head blocks * 60416 B), each rounded to 256 B
     b, h, s = 64, 64, 4
     rows = b * s * h
     r256 = lambda n: ((n + 255) // 256) * 256

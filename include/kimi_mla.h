@@ -8,10 +8,11 @@
  *
  *      0                  success (KIMI_OK)
  *      negative           bad arguments, detected on the host before launch
- *      1 .. 999           a device status word read back by kimi_device_status
+ *      1 .. 0xFFFF        a device status word read back by kimi_device_status
  *                         (KIMI_DEVICE_* bits: a bounded device wait gave up,
- *                         or a page id lay outside the cache)
- *      >= 1000            a CUDA runtime error from the launch (the cudaError_t
+ *                         a page id lay outside the cache, or a peer rank did
+ *                         not reach an all-reduce barrier in time)
+ *      >= 0x10000         a CUDA runtime error from the launch (the cudaError_t
  *                         value plus KIMI_ERR_CUDA_BASE)
  *
  * Reference interfaces replaced (paths inside the ianye23301/kimi tree):
@@ -76,7 +77,7 @@ extern "C" {
 #define KIMI_MLA_MAX_SPLITS 64
 #define KIMI_MLA_MAX_HEADS 128
 #define KIMI_MLA_STATIC_WORKSPACE_BYTES 33554432u /* 32 MiB, see kimi_mla_decode_static_workspace */
-#define KIMI_ABI_VERSION 200
+#define KIMI_ABI_VERSION 201
 
 /* Bits the decode kernels OR into the caller's device status word
  * (KimiMlaDecodeParams.status).  Every device-side wait of the decode is
@@ -100,6 +101,9 @@ extern "C" {
  * and this bit is set.  The reference indexes the cache tensor with the id
  * and raises an index error (or reads another page for a negative id). */
 #define KIMI_DEVICE_BAD_PAGE        0x200
+/* The two-shot all-reduce (kimi_ar_rmsnorm_mxfp4_two_shot): a rank did not
+ * reach the entry or exit barrier within the call's timeout_ns. */
+#define KIMI_DEVICE_PEER_WAIT       0x400
 
 enum {
   KIMI_OK = 0,
@@ -110,7 +114,7 @@ enum {
   KIMI_ERR_WORKSPACE_TOO_SMALL = -5,
   KIMI_ERR_UNSUPPORTED = -6,
   KIMI_ERR_STATIC_WORKSPACE_LIMIT = -7,
-  KIMI_ERR_CUDA_BASE = 1000
+  KIMI_ERR_CUDA_BASE = 0x10000 /* above every combination of KIMI_DEVICE_* bits */
 };
 
 /* Arguments of one decode call.  Element strides are in elements of the
@@ -301,6 +305,47 @@ typedef struct KimiArRmsNormParams {
 } KimiArRmsNormParams;
 
 KIMI_API int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* params, void* stream);
+
+/* The same step as a two-shot exchange over peer memory, with its own device
+ * barriers (the same reference interface as kimi_ar_rmsnorm_mxfp4).  Every
+ * rank of `world` calls it with the same rows, hidden, eps, weight values and
+ * epoch; rank r computes rows [r rows / world, (r + 1) rows / world) from all
+ * ranks' partials and stores those rows' residual_out, nibbles and scales into
+ * every rank's buffers, so that when the call completes each rank holds all
+ * rows.  The call waits on the device for the other ranks twice (at entry, so
+ * that no partial is read before its rank has written it; at exit, so that no
+ * rank reuses its partial while another still reads it): no host barrier is
+ * needed around it.  Each wait is bounded by timeout_ns (0 = 2 s); a wait
+ * that runs out sets KIMI_DEVICE_PEER_WAIT in *status and leaves the rows of
+ * that call undefined.
+ * Pointer arrays are indexed by rank; all of them are device pointers this
+ * GPU can read and write (its own buffers and peer buffers mapped over
+ * NVLink, for example with CUDA IPC).  flags: every rank's int32
+ * [2 * KIMI_AR_MAX_INPUTS], zero before the first call; counter: this rank's
+ * int32, zero before the first call (each call leaves it zero); epoch: 1 for
+ * the first call, then one more for each call (the same on every rank).  No
+ * TMA or bulk copy touches peer memory: plain loads and stores only. */
+typedef struct KimiArTwoShotParams {
+  const void* inputs[KIMI_AR_MAX_INPUTS];  /* every rank's partial, bf16 [rows, hidden] */
+  void* residual_out[KIMI_AR_MAX_INPUTS];  /* every rank's bf16 [rows, hidden] */
+  void* nibbles[KIMI_AR_MAX_INPUTS];       /* every rank's uint8 [rows, hidden / 2] */
+  void* scales[KIMI_AR_MAX_INPUTS];        /* every rank's uint8 [rows, hidden / 32] */
+  int32_t* flags[KIMI_AR_MAX_INPUTS];      /* every rank's int32 [2 * KIMI_AR_MAX_INPUTS] */
+  int32_t* counter;                        /* this rank's int32 */
+  const void* residual;                    /* this rank's bf16 [rows, hidden] (equal on every rank) */
+  const void* weight;                      /* bf16 [hidden] */
+  float eps;
+  int32_t rows;
+  int32_t hidden;
+  int32_t legacy_rule;
+  int32_t world;                           /* 1 .. KIMI_AR_MAX_INPUTS */
+  int32_t rank;
+  int32_t epoch;
+  int32_t* status;                         /* optional device word (KIMI_DEVICE_PEER_WAIT) */
+  uint64_t timeout_ns;
+} KimiArTwoShotParams;
+
+KIMI_API int kimi_ar_rmsnorm_mxfp4_two_shot(const KimiArTwoShotParams* params, void* stream);
 
 /* The decode step after attention: V up-projection of the heads-first latent
  * output, then o_proj.  Replaces `MLAAttention._v_up_proj_and_o_proj(o,

@@ -13,7 +13,7 @@ import threading
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libkimi_mla.so")
 
 KIMI_OK = 0
-KIMI_ERR_CUDA_BASE = 1000
+KIMI_ERR_CUDA_BASE = 0x10000
 
 # Symbols the header declares; tests check the library exports each one.
 EXPORTED_SYMBOLS = (
@@ -30,15 +30,17 @@ EXPORTED_SYMBOLS = (
     "kimi_mla_decode_merge",
     "kimi_mla_q_absorb_rope_append",
     "kimi_ar_rmsnorm_mxfp4",
+    "kimi_ar_rmsnorm_mxfp4_two_shot",
     "kimi_mla_v_up_o_proj",
     "kimi_device_status",
 )
 
-ABI_VERSION = 200
+ABI_VERSION = 201
 
 # Bits of the decode's device status word (KIMI_DEVICE_* in include/kimi_mla.h).
 DEVICE_WAIT_BITS = 0x1FF
 DEVICE_BAD_PAGE = 0x200
+DEVICE_PEER_WAIT = 0x400
 
 AR_MAX_INPUTS = 8
 
@@ -142,6 +144,28 @@ class KimiArRmsNormParams(ctypes.Structure):
     ]
 
 
+class KimiArTwoShotParams(ctypes.Structure):
+    _fields_ = [
+        ("inputs", ctypes.c_void_p * 8),
+        ("residual_out", ctypes.c_void_p * 8),
+        ("nibbles", ctypes.c_void_p * 8),
+        ("scales", ctypes.c_void_p * 8),
+        ("flags", ctypes.c_void_p * 8),
+        ("counter", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+        ("rows", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("legacy_rule", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("epoch", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_uint64),
+    ]
+
+
 class KimiVUpOProjParams(ctypes.Structure):
     _fields_ = [
         ("o", ctypes.c_void_p),
@@ -200,6 +224,8 @@ def load() -> ctypes.CDLL:
         lib.kimi_mla_q_absorb_rope_append.argtypes = [ctypes.POINTER(KimiQAbsorbParams), vp]
         lib.kimi_ar_rmsnorm_mxfp4.restype = ctypes.c_int
         lib.kimi_ar_rmsnorm_mxfp4.argtypes = [ctypes.POINTER(KimiArRmsNormParams), vp]
+        lib.kimi_ar_rmsnorm_mxfp4_two_shot.restype = ctypes.c_int
+        lib.kimi_ar_rmsnorm_mxfp4_two_shot.argtypes = [ctypes.POINTER(KimiArTwoShotParams), vp]
         lib.kimi_mla_v_up_o_proj.restype = ctypes.c_int
         lib.kimi_mla_v_up_o_proj.argtypes = [ctypes.POINTER(KimiVUpOProjParams), vp]
         lib.kimi_device_status.restype = ctypes.c_int

@@ -21,7 +21,7 @@ static_assert(kimi::kStatusSoftmaxWait == KIMI_DEVICE_SOFTMAX_WAIT && kimi::kSta
                   kimi::kStatusIssuerPvWait == KIMI_DEVICE_ISSUER_PV_WAIT &&
                   kimi::kStatusConverterWait == KIMI_DEVICE_CONVERTER_WAIT && kimi::kStatusDrain == KIMI_DEVICE_DRAIN_WAIT &&
                   kimi::kStatusProducerWait == KIMI_DEVICE_PRODUCER_WAIT && kimi::kStatusBadPage == KIMI_DEVICE_BAD_PAGE &&
-                  kimi::kStatusScaleWait == KIMI_DEVICE_SCALE_WAIT,
+                  kimi::kStatusScaleWait == KIMI_DEVICE_SCALE_WAIT && kimi::kStatusPeerWait == KIMI_DEVICE_PEER_WAIT,
               "device status bits of the kernels and the header agree");
 
 inline bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
@@ -186,6 +186,8 @@ const char* kimi_status_string(int status) {
     default: break;
   }
   if (status > 0 && status < KIMI_ERR_CUDA_BASE) {
+    if (status & KIMI_DEVICE_PEER_WAIT)
+      return "a peer rank did not reach the all-reduce barrier in time (the call's output is not valid)";
     if (status & KIMI_DEVICE_BAD_PAGE)
       return (status & ~KIMI_DEVICE_BAD_PAGE) ? "a device wait gave up; a page id was outside the cache"
                                               : "a page id was outside the cache (its tokens were read as zeros)";
@@ -456,6 +458,47 @@ int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* p, void* stream) {
   return cuda_status(kimi::launch_ar_norm_quant(a, static_cast<cudaStream_t>(stream)));
 }
 
+int kimi_ar_rmsnorm_mxfp4_two_shot(const KimiArTwoShotParams* p, void* stream) {
+  if (!p) return KIMI_ERR_NULL_POINTER;
+  if (p->rows < 0 || p->hidden < 32 || p->hidden % 32 || p->hidden > 8192 || p->world < 1 ||
+      p->world > KIMI_AR_MAX_INPUTS || p->rank < 0 || p->rank >= p->world || !std::isfinite(p->eps) || p->eps < 0.f)
+    return KIMI_ERR_BAD_SHAPE;
+  if (p->legacy_rule != 0 && p->legacy_rule != 1) return KIMI_ERR_UNSUPPORTED;
+  if (!p->counter || !p->residual || !p->weight) return KIMI_ERR_NULL_POINTER;
+  if (!aligned(p->counter, 4) || !aligned(p->residual, 16) || !aligned(p->weight, 16) ||
+      (p->status && !aligned(p->status, 4)))
+    return KIMI_ERR_MISALIGNED;
+  kimi::ArTwoShotArgs t{};
+  for (int r = 0; r < kimi::kArMaxInputs; ++r) {
+    if (r >= p->world) break;
+    if (!p->inputs[r] || !p->residual_out[r] || !p->nibbles[r] || !p->scales[r] || !p->flags[r])
+      return KIMI_ERR_NULL_POINTER;
+    if (!aligned(p->inputs[r], 16) || !aligned(p->residual_out[r], 16) || !aligned(p->nibbles[r], 16) ||
+        !aligned(p->flags[r], 4))
+      return KIMI_ERR_MISALIGNED;
+    t.base.inputs[r] = static_cast<const __nv_bfloat16*>(p->inputs[r]);
+    t.residual_out[r] = static_cast<__nv_bfloat16*>(p->residual_out[r]);
+    t.nibbles[r] = static_cast<uint8_t*>(p->nibbles[r]);
+    t.scales[r] = static_cast<uint8_t*>(p->scales[r]);
+    t.flags[r] = p->flags[r];
+  }
+  t.base.num_inputs = p->world;
+  t.base.residual = static_cast<const __nv_bfloat16*>(p->residual);
+  t.base.weight = static_cast<const __nv_bfloat16*>(p->weight);
+  t.base.eps = p->eps;
+  t.base.rows = p->rows;
+  t.base.hidden = p->hidden;
+  t.base.legacy_rule = p->legacy_rule;
+  t.counter = p->counter;
+  t.status = p->status;
+  t.timeout_ns = p->timeout_ns ? p->timeout_ns : kimi::kDefaultTimeoutNs;
+  t.world = p->world;
+  t.rank = p->rank;
+  t.epoch = p->epoch;
+  // zero rows still take part in both barriers (every rank makes the same calls)
+  return cuda_status(kimi::launch_ar_two_shot(t, static_cast<cudaStream_t>(stream)));
+}
+
 int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* p, void* stream) {
   if (!p) return KIMI_ERR_NULL_POINTER;
   if (p->num_tokens < 0 || p->num_heads < 1 || p->num_heads > 8 || p->hidden < 64 || p->hidden % 64)
@@ -517,7 +560,7 @@ int kimi_device_status(int32_t* device_word, int32_t clear, void* stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e == cudaSuccess && clear) e = cudaMemsetAsync(device_word, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return cuda_status(e);
-  return host & 0x3FF;
+  return host & 0x7FF;
 }
 
 int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,

@@ -66,12 +66,25 @@ __device__ __forceinline__ void warp_regroup(uint4 (&v)[4], uint4* stage, int la
   __syncwarp();
 }
 
+// Where one row's results go: `n` copies of residual_out / nibbles / scales
+// (the local buffers, or every rank's for the two-shot form), all written
+// with the same values.
+struct RowDest {
+  __nv_bfloat16* residual_out[kArMaxInputs];
+  uint8_t* nibbles[kArMaxInputs];
+  uint8_t* scales[kArMaxInputs];
+  int n;
+};
+
+// Row `row` of a: the inputs summed in rank order, the residual added, the
+// new residual, RMSNorm and MXFP4 of the row stored to every destination of
+// `d`.  One CTA of ((hidden / 32 + 31) / 32) * 32 threads.
 template <bool LEGACY>
-__global__ void __launch_bounds__(256) ar_norm_quant_kernel(const __grid_constant__ ArNormArgs a) {
+__device__ __forceinline__ void norm_quant_row(const ArNormArgs& a, int row, const RowDest& d) {
   __shared__ float warp_sum[32];
   __shared__ float rstd;
   __shared__ uint4 stage[8][128];  // one 2 KB regroup stage per warp (at most 256 threads)
-  const int row = blockIdx.x, g = threadIdx.x, lane = g & 31, warp = g >> 5;
+  const int g = threadIdx.x, lane = g & 31, warp = g >> 5;
   const int groups = a.hidden / 32;
   const bool live = g < groups;
   const int64_t off = static_cast<int64_t>(row) * a.hidden + 32 * g;
@@ -133,9 +146,13 @@ __global__ void __launch_bounds__(256) ar_norm_quant_kernel(const __grid_constan
       const __nv_bfloat162 pr = __floats2bfloat162_rn(c[2 * j], c[2 * j + 1]);
       packed[j] = *reinterpret_cast<const uint32_t*>(&pr);
     }
-    uint4* ro = reinterpret_cast<uint4*>(a.residual_out + off);
+#pragma unroll 1
+    for (int k = 0; k < d.n; ++k) {
+      uint4* ro = reinterpret_cast<uint4*>(d.residual_out[k] + off);
 #pragma unroll
-    for (int p = 0; p < 4; ++p) ro[p] = make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
+      for (int p = 0; p < 4; ++p)
+        ro[p] = make_uint4(packed[4 * p], packed[4 * p + 1], packed[4 * p + 2], packed[4 * p + 3]);
+    }
 #pragma unroll
     for (int i = 0; i < 32; ++i) sq = __fadd_rn(sq, __fmul_rn(c[i], c[i]));
   }
@@ -164,12 +181,152 @@ __global__ void __launch_bounds__(256) ar_norm_quant_kernel(const __grid_constan
   uint32_t nib[4];
   uint8_t sb;
   quantize_group32<LEGACY>(out, nib, sb);
-  *reinterpret_cast<uint4*>(a.nibbles + static_cast<int64_t>(row) * (a.hidden / 2) + 16 * g) =
-      make_uint4(nib[0], nib[1], nib[2], nib[3]);
-  a.scales[static_cast<int64_t>(row) * groups + g] = sb;
+#pragma unroll 1
+  for (int k = 0; k < d.n; ++k) {
+    *reinterpret_cast<uint4*>(d.nibbles[k] + static_cast<int64_t>(row) * (a.hidden / 2) + 16 * g) =
+        make_uint4(nib[0], nib[1], nib[2], nib[3]);
+    d.scales[k][static_cast<int64_t>(row) * groups + g] = sb;
+  }
+}
+
+template <bool LEGACY>
+__global__ void __launch_bounds__(256) ar_norm_quant_kernel(const __grid_constant__ ArNormArgs a) {
+  RowDest d;
+  d.residual_out[0] = a.residual_out;
+  d.nibbles[0] = a.nibbles;
+  d.scales[0] = a.scales;
+  d.n = 1;
+  norm_quant_row<LEGACY>(a, blockIdx.x, d);
+}
+
+// ---------------------------------------------------------------------------
+// Two-shot form over peer memory
+// ---------------------------------------------------------------------------
+// Rank r computes rows [r R / N, (r + 1) R / N) of the R rows -- each row
+// reading all N ranks' partials, as above -- and stores each row's results
+// into every rank's output buffers (plain peer stores).  Per call each rank
+// reads 1 / N of every partial and writes its rows N times, instead of every
+// rank reading all N partials whole.
+//
+// Two flag barriers over the ranks' flag words (int32 [2][N] per rank, slot
+// [phase][source rank]; a rank writes the call's epoch into every rank's
+// slot, and waits until its own N slots of the phase hold it):
+//   * entry: a rank's partial is complete when its call starts (stream
+//     order); nobody reads a partial before all N ranks have entered;
+//   * exit: the last CTA of a rank to finish its rows (a counter in the
+//     rank's memory) announces that the rank's stores are out and its reads
+//     done, then waits for all ranks: when the call completes, every rank's
+//     rows have landed here and no rank still reads this rank's partial.
+// Epochs only grow, so the flags are never reset.  Every wait is bounded in
+// time; a wait that runs out sets kStatusPeerWait in the status word (after
+// an entry give-up the CTA neither reads nor stores a row).  The ranks' flags
+// may then be out of step: the exchange is to be set up anew.
+// One system-scope fence per signal and per wait, made by one thread: a
+// fence.sc.sys costs microseconds here, so the CTA's stores are first
+// ordered before thread 0 by the CTA barrier (a release is cumulative over
+// what precedes it in causality order), thread 0 fences once and writes the
+// flags with relaxed stores; a waiting thread polls with relaxed loads and
+// fences once it has seen the value (the acquire pattern).
+__device__ __forceinline__ void st_relaxed_sys(int* p, int v) {
+  asm volatile("st.relaxed.sys.global.b32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_relaxed_sys(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;\n" ::: "memory"); }
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+// Thread 0 (after a CTA barrier): this rank's slot of `phase` in every rank's
+// flag words := the epoch.
+__device__ __forceinline__ void signal_all_ranks(const ArTwoShotArgs& t, int phase) {
+  fence_acq_rel_sys();
+  for (int r = 0; r < t.world; ++r) st_relaxed_sys(t.flags[r] + phase * kArMaxInputs + t.rank, t.epoch);
+}
+
+// Threads 0 .. world - 1 each wait for one rank's slot of `phase` to reach
+// the epoch (epochs are compared as the difference, so they may wrap); the
+// CTA's verdict is the AND over them.
+__device__ __forceinline__ bool wait_all_ranks(const ArTwoShotArgs& t, int phase) {
+  __shared__ int failed;
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) < t.world) {
+    const int* slot = t.flags[t.rank] + phase * kArMaxInputs + threadIdx.x;
+    if (ld_relaxed_sys(slot) - t.epoch < 0) {
+      const uint64_t t0 = global_ns();
+      while (ld_relaxed_sys(slot) - t.epoch < 0) {
+        if (global_ns() - t0 >= t.timeout_ns) {
+          atomicExch(&failed, 1);
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    fence_acq_rel_sys();
+  }
+  __syncthreads();
+  const bool ok = failed == 0;
+  if (!ok && threadIdx.x == 0 && t.status) atomicOr(t.status, kStatusPeerWait);
+  return ok;
+}
+
+template <bool LEGACY>
+__global__ void __launch_bounds__(256) ar_two_shot_kernel(const __grid_constant__ ArTwoShotArgs t) {
+  const int begin = static_cast<int>(static_cast<int64_t>(t.base.rows) * t.rank / t.world);
+  const int end = static_cast<int>(static_cast<int64_t>(t.base.rows) * (t.rank + 1) / t.world);
+  // entry: CTA 0 announces this rank (its partial is complete: stream order),
+  // every CTA waits for all ranks.  A CTA whose wait gave up skips its row but
+  // still counts itself below, so the counter stays in step.
+  if (blockIdx.x == 0 && threadIdx.x == 0) signal_all_ranks(t, 0);
+  const bool entered = wait_all_ranks(t, 0);
+  const int row = begin + static_cast<int>(blockIdx.x);
+  if (entered && row < end) {
+    RowDest d;
+#pragma unroll
+    for (int k = 0; k < kArMaxInputs; ++k) {
+      d.residual_out[k] = t.residual_out[k];
+      d.nibbles[k] = t.nibbles[k];
+      d.scales[k] = t.scales[k];
+    }
+    d.n = t.world;
+    norm_quant_row<LEGACY>(t.base, row, d);
+  }
+  // exit: the CTA's stores are ordered before thread 0 by the barrier; the
+  // rank's last CTA announces the rank (one system fence) and waits for all
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) {
+    int done;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(done) : "l"(t.counter) : "memory");
+    last = done == static_cast<int>(gridDim.x) - 1;
+    if (last) {
+      *t.counter = 0;  // the next call is stream-ordered after this one
+      signal_all_ranks(t, 1);
+    }
+  }
+  __syncthreads();
+  if (last) wait_all_ranks(t, 1);
 }
 
 }  // namespace
+
+cudaError_t launch_ar_two_shot(const ArTwoShotArgs& t, cudaStream_t stream) {
+  const int threads = ((t.base.hidden / 32) + 31) / 32 * 32;
+  const int mine = static_cast<int>(static_cast<int64_t>(t.base.rows) * (t.rank + 1) / t.world -
+                                    static_cast<int64_t>(t.base.rows) * t.rank / t.world);
+  const int grid = mine > 0 ? mine : 1;  // a rank without rows still takes part in both barriers
+  if (t.base.legacy_rule)
+    ar_two_shot_kernel<true><<<grid, threads, 0, stream>>>(t);
+  else
+    ar_two_shot_kernel<false><<<grid, threads, 0, stream>>>(t);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ar_norm_quant(const ArNormArgs& a, cudaStream_t stream) {
   const int threads = ((a.hidden / 32) + 31) / 32 * 32;

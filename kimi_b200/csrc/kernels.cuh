@@ -39,6 +39,7 @@ enum : int {
   kStatusDrain = 128,
   kStatusProducerWait = 256,
   kStatusBadPage = 512,
+  kStatusPeerWait = 1024,
   kStatusScaleWait = 8,
 };
 // Default bound of a device wait when the caller passes 0 (2 s).
@@ -100,6 +101,24 @@ struct ArNormArgs {
   int rows;
   int hidden;
   int legacy_rule;
+};
+
+// Two-shot all-reduce + RMSNorm + MXFP4 over peer memory (ar_norm_quant.cu):
+// `base` holds every rank's partial in inputs[] (rank order), this rank's
+// residual, the weight, eps, rows, hidden and the rounding rule; its
+// residual_out / nibbles / scales are unused.
+struct ArTwoShotArgs {
+  ArNormArgs base;
+  __nv_bfloat16* residual_out[kArMaxInputs];  // every rank's [rows, hidden]
+  uint8_t* nibbles[kArMaxInputs];             // every rank's [rows, hidden / 2]
+  uint8_t* scales[kArMaxInputs];              // every rank's [rows, hidden / 32]
+  int* flags[kArMaxInputs];                   // every rank's flag words [2][kArMaxInputs]
+  int* counter;                               // this rank's CTA counter (0 between calls)
+  int* status;                                // optional device word (kStatusPeerWait)
+  unsigned long long timeout_ns;              // bound of each barrier wait
+  int world;
+  int rank;
+  int epoch;                                  // the call's number, the same on every rank
 };
 
 struct VUpOProjArgs {
@@ -204,6 +223,7 @@ struct ReduceArgs {
 cudaError_t launch_kv_append(const KvAppendArgs& a, cudaStream_t stream);
 cudaError_t launch_q_absorb(const QAbsorbArgs& a, cudaStream_t stream);
 cudaError_t launch_ar_norm_quant(const ArNormArgs& a, cudaStream_t stream);
+cudaError_t launch_ar_two_shot(const ArTwoShotArgs& t, cudaStream_t stream);
 cudaError_t launch_v_up_o_proj(const VUpOProjArgs& a, const VUpOProjMaps& maps, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream);

@@ -10,12 +10,19 @@ of it, reading the ranks' partials straight from their buffers.
 
 * :func:`ar_rmsnorm_mxfp4` runs the kernel on a list of partial buffers the
   current GPU can read (its own, and peers' mapped over NVLink).
-* :class:`PeerPartials` maps every rank's partial buffer into every rank
-  (CUDA IPC handles exchanged through ``torch.distributed``, each opened with
-  the reading GPU current, so that GPU's kernels may read it) and orders the
-  kernel between two stream-ordered barriers: the partials are complete
-  before any rank reads them, and no rank overwrites its partial until every
-  rank has read it.  The kernel itself waits for nothing.
+* :class:`PeerPartials` maps every rank's exchange buffer (its partial, the
+  two-shot outputs and flag words) into every rank (CUDA IPC handles
+  exchanged through ``torch.distributed``, each opened with the reading GPU
+  current, so that GPU's kernels may read it).  Two forms:
+
+  - :meth:`PeerPartials.reduce_norm_quant` (one-shot): every rank reads every
+    partial whole; the kernel waits for nothing, so it runs between two
+    stream-ordered barriers (the partials are complete before any rank reads
+    them, and no rank overwrites its partial until every rank has read it);
+  - :meth:`PeerPartials.reduce_norm_quant_two_shot`: rank r reduces, norms
+    and quantises 1 / N of the rows from all partials and stores them into
+    every rank's outputs (``kimi_ar_rmsnorm_mxfp4_two_shot``), with the two
+    barriers done on the device over flag words in peer memory.
 """
 from __future__ import annotations
 
@@ -82,6 +89,19 @@ def _check_cuda(err, what):
         raise RuntimeError(f"{what} failed: CUDA error {int(err)}")
 
 
+def _exchange_layout(rows: int, hidden: int) -> dict:
+    """Byte offsets of the regions of a rank's exchange buffer."""
+    a16 = lambda n: (n + 15) // 16 * 16
+    off, pos = {}, 0
+    for name, nbytes in (("partial", rows * hidden * 2), ("residual_out", rows * hidden * 2),
+                         ("nibbles", rows * hidden // 2), ("scales", rows * hidden // 32),
+                         ("flags", 2 * _lib.AR_MAX_INPUTS * 4)):
+        off[name] = pos
+        pos += a16(nbytes)
+    off["total"] = pos
+    return off
+
+
 class CudaIpc:
     """The CUDA IPC calls :class:`PeerPartials` makes (cuda-python bindings).
 
@@ -123,16 +143,20 @@ class CudaIpc:
 
 
 class PeerPartials:
-    """One partial buffer bf16 [rows, hidden] per rank, mapped into every rank.
+    """One exchange buffer per rank, mapped into every rank.
 
     Collective constructor (every rank of ``group`` calls it with the same
-    shape): each rank allocates its buffer, and the buffers' CUDA IPC handles
-    are exchanged with ``all_gather_object``.  ``local`` is this rank's buffer
-    (the o_proj output is written there); ``ptrs`` are every rank's buffer as
-    device addresses this rank's GPU reads (rank order);
-    :meth:`reduce_norm_quant` runs the fused kernel over them between two
-    barriers; :meth:`close` (collective) unmaps the peers' buffers.  ``ipc``
-    is the IPC layer (:class:`CudaIpc` unless another is given).
+    shape): each rank allocates its buffer -- its partial bf16 [rows, hidden],
+    the two-shot outputs (``residual_out``, ``nibbles``, ``scales``) and its
+    flag words -- and the buffers' CUDA IPC handles are exchanged with
+    ``all_gather_object``.  ``local`` is this rank's partial (the o_proj
+    output is written there); ``ptrs`` are every rank's partial and ``bases``
+    every rank's buffer, as device addresses this rank's GPU reads (rank
+    order).  :meth:`reduce_norm_quant` runs the one-shot kernel between two
+    host-ordered barriers, :meth:`reduce_norm_quant_two_shot` the two-shot
+    kernel with its device barriers; :meth:`close` (collective) unmaps the
+    peers' buffers.  ``ipc`` is the IPC layer (:class:`CudaIpc` unless
+    another is given).
     """
 
     def __init__(self, rows: int, hidden: int, device: torch.device, group=None, ipc=None):
@@ -143,11 +167,24 @@ class PeerPartials:
         self.world = dist.get_world_size(group)
         if self.world > _lib.AR_MAX_INPUTS:
             raise ValueError(f"at most {_lib.AR_MAX_INPUTS} ranks")
+        if hidden % 32:
+            raise ValueError("hidden must be a multiple of 32")
         self.ipc = ipc if ipc is not None else CudaIpc()
         self.device = torch.device(device)
         self.rows, self.hidden = rows, hidden
-        self.local = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=self.device)
-        ptr = self.local.data_ptr()
+        # one allocation (one IPC handle): the partial, then the two-shot
+        # outputs and this rank's flag words, each region 16-byte aligned
+        self._off = _exchange_layout(rows, hidden)
+        self.buffer = torch.zeros(self._off["total"], dtype=torch.uint8, device=self.device)
+        self.local = self._region("partial", torch.bfloat16, (rows, hidden))
+        self.residual_out = self._region("residual_out", torch.bfloat16, (rows, hidden))
+        self.nibbles = self._region("nibbles", torch.uint8, (rows, hidden // 2))
+        self.scales = self._region("scales", torch.uint8, (rows, hidden // 32))
+        # this rank's CTA counter and device status word (not shared)
+        self._words = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.status = self._words[1:2]
+        self.epoch = 0
+        ptr = self.buffer.data_ptr()
         # Every rank joins the gather even when its export failed (an
         # allocation from PYTORCH_CUDA_ALLOC_CONF=expandable_segments has no
         # IPC handle, for one): each sends (ok, payload) and all of them raise
@@ -165,18 +202,26 @@ class PeerPartials:
         # open every peer's allocation with this rank's GPU current: the mapping
         # (and the peer access it enables) belongs to this GPU's context
         self.ipc.make_current(self.device)
-        self._opened, self.ptrs = [], []
+        self._opened, self.ptrs, self.bases = [], [], []
         try:
             for r, (_, (raw, offset)) in enumerate(shared):
                 if r == self.rank:
-                    self.ptrs.append(ptr)
-                    continue
-                base = self.ipc.open(raw)
-                self._opened.append(base)
-                self.ptrs.append(base + offset)
+                    self.bases.append(ptr)
+                else:
+                    base = self.ipc.open(raw)
+                    self._opened.append(base)
+                    self.bases.append(base + offset)
+                self.ptrs.append(self.bases[-1] + self._off["partial"])
         except Exception:
             self._unmap()
             raise
+
+    def _region(self, name: str, dtype: torch.dtype, shape) -> torch.Tensor:
+        n = 1
+        for d in shape:
+            n *= d
+        start = self._off[name]
+        return self.buffer[start:start + n * torch.empty(0, dtype=dtype).element_size()].view(dtype).view(*shape)
 
     def _unmap(self):
         """Close every mapping this rank opened; the first failure is raised
@@ -187,7 +232,7 @@ class PeerPartials:
                 self.ipc.close(b)
             except Exception as e:  # noqa: BLE001 - re-raised below
                 first = first or e
-        self._opened, self.ptrs = [], []
+        self._opened, self.ptrs, self.bases = [], [], []
         if first is not None:
             raise first
 
@@ -224,3 +269,45 @@ class PeerPartials:
         out = ar_rmsnorm_mxfp4(self.ptrs, residual, weight, eps, residual_out=residual_out, legacy_rule=legacy_rule)
         self._barrier()  # every rank has read every partial
         return out
+
+    def reduce_norm_quant_two_shot(self, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                                   legacy_rule: bool = False, timeout_ns: int = 0):
+        """The same result as :meth:`reduce_norm_quant` for the first
+        ``residual.shape[0]`` rows, as a two-shot exchange: this rank reduces
+        1 / N of the rows from every partial and stores them into every rank's
+        outputs, the ranks meeting at two device barriers (no host barrier).
+        Collective: every rank calls it, in the same order, with the same
+        shapes.  Returns views of this rank's outputs ``(residual_out [rows,
+        hidden], nibbles [rows, hidden/2], scales [rows, hidden/32])``, valid
+        until the next call.  A barrier wait that runs out (``timeout_ns``, 0 =
+        2 s) sets ``_lib.DEVICE_PEER_WAIT`` in ``self.status`` (read it with
+        :func:`kimi_b200.device_status`); the exchange is then to be set up
+        anew."""
+        rows = residual.shape[0] if residual.dim() == 2 else -1
+        if rows < 0 or rows > self.rows or residual.shape[1] != self.hidden:
+            raise ValueError(f"residual must be [<= {self.rows}, {self.hidden}]")
+        if residual.dtype != torch.bfloat16 or not residual.is_contiguous():
+            raise ValueError("residual must be a contiguous bf16 tensor")
+        if weight.dtype != torch.bfloat16 or weight.shape != (self.hidden,) or not weight.is_contiguous():
+            raise ValueError("weight must be a contiguous bf16 [hidden] tensor")
+        if not self.bases:
+            raise RuntimeError("PeerPartials is closed")
+        self.epoch += 1
+        p = _lib.KimiArTwoShotParams()
+        for r, base in enumerate(self.bases):
+            p.inputs[r] = base + self._off["partial"]
+            p.residual_out[r] = base + self._off["residual_out"]
+            p.nibbles[r] = base + self._off["nibbles"]
+            p.scales[r] = base + self._off["scales"]
+            p.flags[r] = base + self._off["flags"]
+        p.counter = self._words.data_ptr()
+        p.residual, p.weight = residual.data_ptr(), weight.data_ptr()
+        p.eps = float(eps)
+        p.rows, p.hidden, p.legacy_rule = rows, self.hidden, int(bool(legacy_rule))
+        p.world, p.rank, p.epoch = self.world, self.rank, self.epoch
+        p.status = self.status.data_ptr()
+        p.timeout_ns = int(timeout_ns)
+        with torch.cuda.device(self.device):
+            st = _lib.load().kimi_ar_rmsnorm_mxfp4_two_shot(ctypes.byref(p), _stream_handle(self.device))
+        _lib.check(st, "kimi_ar_rmsnorm_mxfp4_two_shot")
+        return self.residual_out[:rows], self.nibbles[:rows], self.scales[:rows]

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_status_strings_and_version():
     lib = _lib.load()
-    assert lib.kimi_abi_version() == _lib.ABI_VERSION == 200
+    assert lib.kimi_abi_version() == _lib.ABI_VERSION == 201
     assert _lib.status_text(0) == "ok"
     assert "workspace" in _lib.status_text(-5)
     assert _lib.status_text(-12345) == "unknown status"
@@ -44,6 +44,10 @@ def test_device_status_texts():
     assert "outside the cache" in bad and "gave up" not in bad
     both = _lib.status_text(_lib.DEVICE_BAD_PAGE | 0x040)
     assert "gave up" in both and "outside the cache" in both
+    assert "peer rank" in _lib.status_text(_lib.DEVICE_PEER_WAIT)
+    # every combination of device bits stays below the CUDA error range
+    assert "gave up" in _lib.status_text(0x3FF) and "peer rank" in _lib.status_text(0x7FF)
+    assert 0x7FF < _lib.KIMI_ERR_CUDA_BASE
     # CUDA errors keep their own range
     assert "gave up" not in _lib.status_text(_lib.KIMI_ERR_CUDA_BASE + 2)
 

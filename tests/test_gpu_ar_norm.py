@@ -2,9 +2,9 @@
 (kimi_ar_rmsnorm_mxfp4 through the C ABI) against the CPU oracle: the new
 residual, the MXFP4 nibbles and the e8m0 scales bit-exact (the kernel and the
 oracle take the same float32 steps in the same order).  The ranks' partials
-are separate buffers on this GPU; a two-process run over two GPUs, reading
-the peer's buffer through a CUDA IPC mapping, runs where two GPUs are
-visible."""
+are separate buffers on this GPU; runs of 2 and 8 processes over as many
+GPUs, reading the peers' buffers through CUDA IPC mappings, check both the
+one-shot and the two-shot form where that many GPUs are visible."""
 import os
 import socket
 
@@ -16,6 +16,7 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 from kimi_b200 import tp  # noqa: E402
+import kimi_b200  # noqa: E402
 from oracle import ar_norm  # noqa: E402
 from oracle import mxfp4 as omx  # noqa: E402
 
@@ -78,39 +79,167 @@ def test_residual_updated_in_place():
     np.testing.assert_array_equal(g_nib.cpu().numpy(), nib)
 
 
-def _two_rank_worker(rank, world, port, result_dir):
+# ---------------------------------------------------------------------------
+# two-shot form (kimi_ar_rmsnorm_mxfp4_two_shot)
+# ---------------------------------------------------------------------------
+def _two_shot_params(world, rank, parts, outs, flags, counter, res, w, rows, hidden, epoch, status=None,
+                     timeout_ns=0):
+    from kimi_b200 import _lib
+    p = _lib.KimiArTwoShotParams()
+    for r in range(world):
+        p.inputs[r] = parts[r].data_ptr()
+        p.residual_out[r], p.nibbles[r], p.scales[r] = (t.data_ptr() for t in outs[r])
+        p.flags[r] = flags[r].data_ptr()
+    p.counter = counter.data_ptr()
+    p.residual, p.weight = res.data_ptr(), w.data_ptr()
+    p.eps, p.rows, p.hidden, p.legacy_rule = 1e-6, rows, hidden, 0
+    p.world, p.rank, p.epoch = world, rank, epoch
+    p.status = status.data_ptr() if status is not None else None
+    p.timeout_ns = timeout_ns
+    return p
+
+
+def _outs(rows, hidden, dev=DEV):
+    return (torch.zeros(rows, hidden, dtype=torch.bfloat16, device=dev),
+            torch.zeros(rows, hidden // 2, dtype=torch.uint8, device=dev),
+            torch.zeros(rows, hidden // 32, dtype=torch.uint8, device=dev))
+
+
+def test_two_shot_one_rank_matches_oracle_over_several_epochs():
+    """One rank: both barriers meet at once; three calls (epochs 1..3) on new
+    inputs, each bit-exact against the oracle, the counter left at zero."""
+    import ctypes
+    from kimi_b200 import _lib
+    lib = _lib.load()
+    rows, hidden = 37, 7168
+    flags = [torch.zeros(16, dtype=torch.int32, device=DEV)]
+    counter = torch.zeros(1, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    outs = [_outs(rows, hidden)]
+    for epoch in (1, 2, 3):
+        rng = np.random.default_rng(90 + epoch)
+        x, res, w = _bf16_np(rng, (rows, hidden)), _bf16_np(rng, (rows, hidden)), _bf16_np(rng, (hidden,))
+        part, rt, wt = _t(x), _t(res), _t(w)
+        p = _two_shot_params(1, 0, [part], outs, flags, counter, rt, wt, rows, hidden, epoch, status)
+        st = lib.kimi_ar_rmsnorm_mxfp4_two_shot(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
+        assert st == 0, _lib.status_text(st)
+        torch.cuda.synchronize()
+        comb, _, nib, sc = ar_norm.ar_rmsnorm_mxfp4([x], res, w, 1e-6)
+        np.testing.assert_array_equal(_bits(outs[0][0]), comb)
+        np.testing.assert_array_equal(outs[0][1].cpu().numpy(), nib)
+        np.testing.assert_array_equal(outs[0][2].cpu().numpy(), sc)
+    assert counter.item() == 0 and status.item() == 0
+    assert flags[0].cpu().tolist()[:1] == [3] and flags[0].cpu().tolist()[8:9] == [3]
+
+
+def test_two_shot_missing_rank_runs_out_and_reports():
+    """Rank 0 of two, with rank 1 never called (its flag words are local
+    memory nothing writes): the entry wait runs out (0.2 ms), no row is
+    computed, the exit wait runs out too, the status word carries
+    DEVICE_PEER_WAIT and the stream stays usable."""
+    import ctypes
+    from kimi_b200 import _lib
+    lib = _lib.load()
+    rows, hidden = 16, 256
+    parts = [torch.zeros(rows, hidden, dtype=torch.bfloat16, device=DEV) for _ in range(2)]
+    outs = [_outs(rows, hidden) for _ in range(2)]
+    flags = [torch.zeros(16, dtype=torch.int32, device=DEV) for _ in range(2)]
+    counter = torch.zeros(1, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    res = torch.ones(rows, hidden, dtype=torch.bfloat16, device=DEV)
+    w = torch.ones(hidden, dtype=torch.bfloat16, device=DEV)
+    p = _two_shot_params(2, 0, parts, outs, flags, counter, res, w, rows, hidden, 1, status, timeout_ns=200_000)
+    st = lib.kimi_ar_rmsnorm_mxfp4_two_shot(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    bits = kimi_b200.device_status(status)
+    assert bits == _lib.DEVICE_PEER_WAIT, hex(bits)
+    assert torch.count_nonzero(outs[0][0]).item() == 0  # nothing was computed
+    assert counter.item() == 0
+    torch.ones(4, device=DEV).sum().item()  # the context still works
+
+
+def _ranks_worker(rank, world, port, result_dir):
+    """Both forms on `world` GPUs, [128, 7168]: bit-exact against the oracle
+    for three different inputs (two-shot epochs 1..3), then each form timed
+    with CUDA events over 50 calls replayed from a CUDA graph (the two-shot
+    call with its device barriers; the one-shot kernel without the host
+    barriers it needs) -- written to the result file."""
+    import datetime
+    import json
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    import datetime
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
+    result = {"ok": True}
     try:
-        rng = np.random.default_rng(80)
         rows, hidden = 128, 7168
-        ins = [_bf16_np(rng, (rows, hidden), 0.5) for _ in range(world)]
-        res, w = _bf16_np(rng, (rows, hidden)), _bf16_np(rng, (hidden,))
         peers = tp.PeerPartials(rows, hidden, dev)
-        peers.local.copy_(_t(ins[rank], dev))
-        r_out, nib, sc = peers.reduce_norm_quant(_t(res, dev), _t(w, dev), 1e-6)
-        torch.cuda.synchronize()
-        comb, _, nib_ref, sc_ref = ar_norm.ar_rmsnorm_mxfp4(ins, res, w, 1e-6)
-        ok = (np.array_equal(_bits(r_out), comb) and np.array_equal(nib.cpu().numpy(), nib_ref)
-              and np.array_equal(sc.cpu().numpy(), sc_ref))
-        with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
-            f.write("ok" if ok else "mismatch")
+        for it in range(3):
+            rng = np.random.default_rng(200 + it)
+            ins = [_bf16_np(rng, (rows, hidden), 0.5) for _ in range(world)]
+            res, w = _bf16_np(rng, (rows, hidden)), _bf16_np(rng, (hidden,))
+            comb, _, nib_ref, sc_ref = ar_norm.ar_rmsnorm_mxfp4(ins, res, w, 1e-6)
+            peers.local.copy_(_t(ins[rank], dev))
+            rt, wt = _t(res, dev), _t(w, dev)
+            r1, n1, s1 = peers.reduce_norm_quant(rt, wt, 1e-6)
+            torch.cuda.synchronize()
+            one_ok = (np.array_equal(_bits(r1), comb) and np.array_equal(n1.cpu().numpy(), nib_ref)
+                      and np.array_equal(s1.cpu().numpy(), sc_ref))
+            r2, n2, s2 = peers.reduce_norm_quant_two_shot(rt, wt, 1e-6)
+            torch.cuda.synchronize()
+            two_ok = (np.array_equal(_bits(r2), comb) and np.array_equal(n2.cpu().numpy(), nib_ref)
+                      and np.array_equal(s2.cpu().numpy(), sc_ref))
+            result["ok"] = result["ok"] and one_ok and two_ok
+            result.setdefault("one_shot_ok", []).append(one_ok)
+            result.setdefault("two_shot_ok", []).append(two_ok)
+        result["status"] = kimi_b200.device_status(peers.status)
+        result["ok"] = result["ok"] and result["status"] == 0
+        # timing: 50 calls captured in a CUDA graph (the two-shot call, whose
+        # barriers are on the device, and the one-shot kernel alone) and
+        # replayed once on every rank together, so the host's launch rate
+        # does not enter; the captured two-shot calls carry the next 50 epochs
+        for name, fn in (("two_shot_us", lambda: peers.reduce_norm_quant_two_shot(rt, wt, 1e-6)),
+                         ("one_shot_kernel_us", lambda: tp.ar_rmsnorm_mxfp4(peers.ptrs, rt, wt, 1e-6))):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(50):
+                    fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            g.replay()
+            e.record()
+            torch.cuda.synchronize()
+            result[name] = s.elapsed_time(e) * 1e3 / 50
+            del g
+        result["status_after_timing"] = kimi_b200.device_status(peers.status)
+        with open(os.path.join(result_dir, f"rank{rank}.json"), "w") as f:
+            json.dump(result, f)
         peers.close()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_ranks_over_nvlink(tmp_path):
+@pytest.mark.parametrize("world", [2, 8])
+def test_ranks_over_nvlink_one_and_two_shot(world, tmp_path):
+    import json
     import torch.multiprocessing as mp
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.start_processes(_two_rank_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
-    for r in range(2):
-        assert (tmp_path / f"rank{r}").read_text() == "ok"
+    mp.start_processes(_ranks_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    results = [json.loads((tmp_path / f"rank{r}.json").read_text()) for r in range(world)]
+    out = os.environ.get("KIMI_AR_TIMING_OUT")
+    if out:  # a summary of the timings (max over ranks), for the profiles
+        with open(out, "a") as f:
+            f.write(json.dumps({"world": world, "two_shot_us": max(r["two_shot_us"] for r in results),
+                                "one_shot_kernel_us": max(r["one_shot_kernel_us"] for r in results)}) + "\n")
+    for r, res in enumerate(results):
+        assert res["ok"], (r, res)
+        assert res["status_after_timing"] == 0, (r, res)

@@ -9,13 +9,18 @@ library's KV-append quantiser).  A step is one decode call over the whole
 batch (one layer).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload kimi_k2|ragged|tp8_prologue|tp8_ar_norm|tp8_vup_oproj]
+                    [--workload kimi_k2|ragged|long|tp8_prologue|tp8_ar_norm|tp8_vup_oproj]
 
 ``--workload ragged`` runs the batch-sharded sweep instead: one batch of 256
 sequences with lengths drawn uniformly from 1K-32K tokens (seeded), spread
 over the N ranks by longest-first bin packing (kimi_b200.dp), each rank
 holding only its sequences' pages; the whole batch is fixed as N grows
 (strong scaling) and the gather of the outputs to rank 0 is timed separately.
+
+``--workload long`` runs the long-context decode of the DeepSeek-V3 shape:
+128 heads, batch 8, 131072 tokens every sequence, 32 splits into
+preallocated partials, one token appended per sequence per step; it reports
+the HBM fraction and the tensor-pipe fraction of the MMA work.
 
 ``--workload tp8_prologue`` times the decode step before attention instead:
 q absorption by W_UK + RoPE + MXFP4 KV append (kimi_b200.q_absorb_rope_append)
@@ -911,13 +916,135 @@ def run_vup(args, rank, world, local_rank):
     }
 
 
+LONG_HEADS, LONG_BATCH, LONG_CTX, LONG_SPLITS = 128, 8, 131072, 32
+LONG_WORKLOAD = (f"DeepSeek-V3-shape MXFP4 MLA decode, long context: {LONG_HEADS} heads, batch {LONG_BATCH}, "
+                 f"ctx {LONG_CTX} every sequence, page {PAGE}, seeded random-permutation page table, "
+                 f"num_kv_splits {LONG_SPLITS} (preallocated partials), one token appended per sequence per step")
+# tensor-core work per token and head: Q K^T as three block-scaled e2m1 terms
+# over the 512 latents (kind::mxf4), q_pe . k_pe in bf16 (64), P V as two
+# e4m3 terms against e5m2 V'' (kind::f8f6f4)
+LONG_FLOPS_MXF4, LONG_FLOPS_BF16, LONG_FLOPS_F8 = 2 * 3 * 512, 2 * 64, 2 * 2 * 512
+
+
+def run_long(args, rank, world, local_rank):
+    """The long-context decode (one GPU; other ranks run their own copy): a
+    step is the append of one token to every sequence plus one decode call
+    over the batch.  Reports the HBM fraction and the tensor-pipe fraction:
+    the MMA work of a step at the measured dense bf16 rate for the bf16 RoPE
+    MMAs, twice it for the fp8 kind and four times it for the fp4 kind (the
+    B200's dense ratios), divided by the measured stage-1 time."""
+    import torch
+
+    import kimi_b200 as kimi
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(17 + rank)
+    pages = LONG_BATCH * LONG_CTX // PAGE
+    kvb, kvs = kimi.alloc_mxfp4_cache(pages, dev, zero=False)
+    chunk = 1 << 16
+    for start in range(0, pages * PAGE, chunk):
+        n = min(chunk, pages * PAGE - start)
+        kv_c = torch.randn(n, 512, generator=gen, device=dev).to(torch.bfloat16)
+        k_pe = torch.randn(n, 64, generator=gen, device=dev).to(torch.bfloat16)
+        kimi.mxfp4_kv_append(kv_c, k_pe, kvb, kvs, torch.arange(start, start + n, device=dev))
+    perm = torch.randperm(pages, generator=gen, device=dev).to(torch.int32)
+    indptr = (torch.arange(LONG_BATCH + 1, device=dev, dtype=torch.int32) * (LONG_CTX // PAGE)).contiguous()
+    last = torch.full((LONG_BATCH,), PAGE, dtype=torch.int32, device=dev)
+    q = torch.randn(LONG_BATCH, LONG_HEADS, 576, generator=gen, device=dev).to(torch.bfloat16)
+    o = torch.empty(LONG_BATCH, LONG_HEADS, 512, dtype=torch.bfloat16, device=dev)
+    ws = kimi.alloc_workspace(LONG_BATCH, LONG_HEADS, LONG_SPLITS, dev)
+    # the appended token: the last slot of each sequence's last page
+    last_pages = perm[indptr[1:].long() - 1].long()
+    slots = last_pages * PAGE + (PAGE - 1)
+    new_c = torch.randn(LONG_BATCH, 512, generator=gen, device=dev).to(torch.bfloat16)
+    new_pe = torch.randn(LONG_BATCH, 64, generator=gen, device=dev).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    call = (q, kvb, kvs, o, None, indptr, perm, last)
+
+    def step():
+        kimi.mxfp4_kv_append(new_c, new_pe, kvb, kvs, slots)
+        kimi.mla_decode_fwd(*call, sm_scale=SM_SCALE, num_kv_splits=LONG_SPLITS, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    steps = args.steps
+    with ClockSampler(dev.index) as clocks:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_step = e0.elapsed_time(e1) / steps
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps)]
+        for i in range(steps):
+            ev[2 * i].record(stream)
+            kimi.mla_decode_partial(*call, sm_scale=SM_SCALE, num_kv_splits=LONG_SPLITS, workspace=ws)
+            ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+        stage1_ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(steps))
+        # end to end: q up from pinned host memory and o back every step
+        q_host = q.cpu().pin_memory()
+        o_host = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            q.copy_(q_host, non_blocking=True)
+            step()
+            o_host.copy_(o, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / steps
+    tokens = LONG_BATCH * LONG_CTX
+    nbytes = algorithmic_bytes(batch=LONG_BATCH, heads=LONG_HEADS, ctx=LONG_CTX)
+    peak, peak_kind = _peak_hbm()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16_tf, tf_kind = float(json.load(f)["bf16_tflops"]), "measured bf16 (burst)"
+    except Exception:
+        bf16_tf, tf_kind = 1590.0, "fallback bf16"
+    per_tok = tokens * LONG_HEADS
+    ideal_ms = (per_tok * LONG_FLOPS_MXF4 / (4 * bf16_tf) + per_tok * LONG_FLOPS_BF16 / bf16_tf +
+                per_tok * LONG_FLOPS_F8 / (2 * bf16_tf)) / 1e9
+    achieved_gbs = nbytes / (stage1_ms * 1e6)
+    if rank != 0:
+        return None
+    return {
+        "metric": "MLA decode µs/layer, achieved HBM TB/s and tensor-pipe fraction (DeepSeek-V3 shape, "
+                  "8 x 131072, 32 splits)",
+        "value": round(nbytes / (ms_step * 1e9), 4), "unit": "TB/s", "n_gpus": 1, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "us_per_layer": round(ms_step * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded normal q and latents, cache written by the library's MXFP4 KV-append)",
+        "config": {"workload": LONG_WORKLOAD, "heads": LONG_HEADS, "batch": LONG_BATCH, "ctx": LONG_CTX,
+                   "num_kv_splits": LONG_SPLITS, "algorithmic_bytes_per_step": nbytes,
+                   "l2": "inputs larger than L2: one 420 MB cache", "parallelism": "dp1"},
+        "e2e": {"value": round(nbytes / (e2e_ms * 1e9), 4), "unit": "TB/s", "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": o.numel() * 2,
+                "path": "q copied up from pinned host memory, append + kimi_b200.mla_decode_fwd, o copied back, "
+                        "in stream order every step"},
+        "gpu_launches": steps * (1 + len(STAGE1_LAUNCHES) + 1),
+        "kernels": {"stage1_ms_median": round(stage1_ms, 5)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved_gbs / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS hbm_gbs)",
+                     "traffic": None},
+        "tensor": {"flops_per_step": per_tok * (LONG_FLOPS_MXF4 + LONG_FLOPS_BF16 + LONG_FLOPS_F8),
+                   "ideal_ms": round(ideal_ms, 5), "frac": round(ideal_ms / stage1_ms, 4),
+                   "peak": f"{tf_kind} {bf16_tf} TFLOP/s for the bf16 MMAs, x2 for kind::f8f6f4, "
+                           f"x4 for kind::mxf4 (the dense fp8/fp4 ratios)"},
+        "clocks": clocks.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "tp8_prologue", "tp8_ar_norm", "tp8_vup_oproj"],
+    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "long", "tp8_prologue", "tp8_ar_norm", "tp8_vup_oproj"],
                     default="kimi_k2")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
                     help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
@@ -942,8 +1069,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        runner = {"tp8_prologue": run_prologue, "tp8_ar_norm": run_ar_norm,
-                  "tp8_vup_oproj": run_vup}.get(args.workload, run_ours)
+        runner = {"tp8_prologue": run_prologue, "tp8_ar_norm": run_ar_norm, "tp8_vup_oproj": run_vup,
+                  "long": run_long}.get(args.workload, run_ours)
         line = runner(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)

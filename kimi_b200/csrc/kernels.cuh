@@ -163,10 +163,12 @@ struct QuantizeArgs {
 // more pieces; a piece that holds a whole sequence writes the final bf16
 // output, any other writes a partial output (normalised by its own softmax
 // sum) and its natural-log log-sum-exp to a workspace slot.
-//   * split mode (balanced = 0): grid (num_splits, batch, head blocks); CTA
+// The grid's x index is (CTA or split) * head blocks + head block: the CTAs of
+// one tile range for the different 64-head blocks are neighbours.
+//   * split mode (balanced = 0): grid (num_splits x head blocks, batch); CTA
 //     (s, b) takes the s-th of num_splits equal tile ranges of sequence b, slot
 //     b * num_splits + s; with one split the CTA writes the output directly.
-//   * balanced mode (balanced = 1): grid (ctas, 1, head blocks); CTA c takes
+//   * balanced mode (balanced = 1): grid (ctas x head blocks, 1); CTA c takes
 //     tiles [c T / ctas, (c + 1) T / ctas) of all T tiles of the batch laid end
 //     to end, slot b + c for its piece of sequence b (unique: along the tile
 //     list both b and c only grow), and the CTA holding a sequence's first tile

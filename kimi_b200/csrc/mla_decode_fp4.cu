@@ -154,6 +154,15 @@ __device__ __forceinline__ uint8_t* smem_base() {
   return dyn_smem;
 }
 
+// The grid's x index interleaves the 64-head blocks fastest: CTA x is head
+// block x % head_blocks of schedule CTA (split) x / head_blocks, so the CTAs
+// that read the same tiles for different head blocks run side by side and
+// the second read is an L2 hit.
+__device__ __forceinline__ int head_blocks(const DecodeArgs& a) { return (a.num_heads + kNH - 1) / kNH; }
+__device__ __forceinline__ int cta_index(const DecodeArgs& a) { return static_cast<int>(blockIdx.x) / head_blocks(a); }
+__device__ __forceinline__ int cta_count(const DecodeArgs& a) { return static_cast<int>(gridDim.x) / head_blocks(a); }
+__device__ __forceinline__ int head_block(const DecodeArgs& a) { return static_cast<int>(blockIdx.x) % head_blocks(a); }
+
 __device__ __forceinline__ void record_status(const DecodeArgs& a, int bits) {
   if (a.status) atomicOr(a.status, bits);
 }
@@ -615,7 +624,7 @@ __device__ void build_q(uint8_t* sm, Misc& ms, uint32_t tmem, const DecodeArgs& 
                         int heads_here, int warp, int lane) {
   const int tid = threadIdx.x;
   if (a.q_img) {
-    const uint8_t* img = a.q_img + (static_cast<int64_t>(b) * gridDim.z + blockIdx.z) * kQImageBytes;
+    const uint8_t* img = a.q_img + (static_cast<int64_t>(b) * head_blocks(a) + head_block(a)) * kQImageBytes;
     asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the Q prep grid is complete (no-op later)
     if (tid == 0) {
       mbar_arrive_expect_tx(&ms.mb_qload, kQTermBytes + kQPeBytes);
@@ -825,8 +834,8 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     // the piece covers its whole sequence -> final output; otherwise a partial in its slot
     const bool direct = a.balanced ? (cur.piece_begin == 0 && cur.piece_end == cursor_tiles(cur))
                                    : a.num_splits == 1;
-    const int64_t slot = a.balanced ? static_cast<int64_t>(cur.b) + blockIdx.x
-                                    : static_cast<int64_t>(cur.b) * a.num_splits + blockIdx.x;
+    const int64_t slot = a.balanced ? static_cast<int64_t>(cur.b) + cta_index(a)
+                                    : static_cast<int64_t>(cur.b) * a.num_splits + cta_index(a);
     named_bar(kBarSoftmax, kSoftmaxThreads);
     if (tid < kNH) {
       const float l = ms.red[0][tid] + ms.red[1][tid] + ms.red[2][tid] + ms.red[3][tid];
@@ -837,8 +846,8 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     }
     if (a.balanced && tid == 0 && cur.piece_begin == 0) {
       // this CTA holds the sequence's first tile: record its CTA span for the merge
-      const int last_cta = cta_of_tile(cur.seq_pos + cursor_tiles(cur) - 1, sc, gridDim.x);
-      a.seq_meta[cur.b] = make_int2(blockIdx.x, last_cta);
+      const int last_cta = cta_of_tile(cur.seq_pos + cursor_tiles(cur) - 1, sc, cta_count(a));
+      a.seq_meta[cur.b] = make_int2(cta_index(a), last_cta);
     }
     named_bar(kBarSoftmax, kSoftmaxThreads);
     // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane.
@@ -900,24 +909,24 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int head_base = blockIdx.z * kNH;
+  const int head_base = head_block(a) * kNH;
   const int heads_here = min(kNH, a.num_heads - head_base);
 
   Sched sc;
   if (a.balanced) {
-    balanced_schedule<kThreads>(a, ms.sched, sc, gridDim.x, blockIdx.x);
+    balanced_schedule<kThreads>(a, ms.sched, sc, cta_count(a), cta_index(a));
     if (sc.count == 0) {
       // An empty run (fewer tiles than CTAs) can sit inside the CTA span of
       // the sequence at its position; its slot of that sequence carries no weight.
       if (sc.pos0 < sc.total && tid < heads_here)
-        a.partial_lse[(static_cast<int64_t>(sc.b0) + blockIdx.x) * a.num_heads + head_base + tid] = -CUDART_INF_F;
+        a.partial_lse[(static_cast<int64_t>(sc.b0) + cta_index(a)) * a.num_heads + head_base + tid] = -CUDART_INF_F;
       return;  // (uniform: every thread read the same count)
     }
   } else {
     const int b = blockIdx.y, tiles = seq_tiles_of(a, b);
     const int per_split = (tiles + a.num_splits - 1) / a.num_splits;
     sc.b0 = b;
-    sc.off0 = blockIdx.x * per_split;
+    sc.off0 = cta_index(a) * per_split;
     sc.count = max(0, min(per_split, tiles - sc.off0));
     sc.pos0 = 0;
     sc.total = 0;
@@ -930,7 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
           *reinterpret_cast<uint32_t*>(a.o + b * a.o_stride_b + (head_base + h) * a.o_stride_h + d) = 0u;
         }
       } else if (tid < heads_here) {
-        a.partial_lse[(static_cast<int64_t>(b) * a.num_splits + blockIdx.x) * a.num_heads + head_base + tid] =
+        a.partial_lse[(static_cast<int64_t>(b) * a.num_splits + cta_index(a)) * a.num_heads + head_base + tid] =
             -CUDART_INF_F;
       }
       return;
@@ -1037,7 +1046,7 @@ cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaSt
   cudaError_t e = cudaFuncSetAttribute(mla_decode_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
   const int head_blocks = (a.num_heads + kNH - 1) / kNH;
-  const dim3 grid = a.balanced ? dim3(a.num_splits, 1, head_blocks) : dim3(a.num_splits, a.batch, head_blocks);
+  const dim3 grid = a.balanced ? dim3(a.num_splits * head_blocks, 1, 1) : dim3(a.num_splits * head_blocks, a.batch, 1);
   if (!a.q_img) {
     mla_decode_fp4_kernel<<<grid, kThreads, kSmem, stream>>>(a, maps);
     return cudaGetLastError();

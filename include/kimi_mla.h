@@ -104,6 +104,12 @@ extern "C" {
 /* The two-shot all-reduce (kimi_ar_rmsnorm_mxfp4_two_shot): a rank did not
  * reach the entry or exit barrier within the call's timeout_ns. */
 #define KIMI_DEVICE_PEER_WAIT       0x400
+/* The decode prologue (kimi_mla_q_absorb_rope_append) and the V up-projection
+ * + o_proj (kimi_mla_v_up_o_proj): a wait gave up.  Their waits keep a fixed
+ * bound of about 2 s (their give-up paths do not wait for the copies and
+ * MMAs already issued, so no shorter caller-set bound is offered). */
+#define KIMI_DEVICE_QABSORB_WAIT    0x800
+#define KIMI_DEVICE_VUP_WAIT        0x1000
 
 enum {
   KIMI_OK = 0,
@@ -272,6 +278,8 @@ typedef struct KimiQAbsorbParams {
   int32_t num_heads;
   int32_t is_neox;
   int32_t legacy_rule;
+  int32_t* status;             /* optional device word: KIMI_DEVICE_QABSORB_WAIT when a wait gave up
+                                  (each wait keeps a fixed ~2 s bound); NULL = not reported */
 } KimiQAbsorbParams;
 
 KIMI_API int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* params, void* stream);
@@ -372,6 +380,8 @@ typedef struct KimiVUpOProjParams {
   int32_t num_tokens;
   int32_t num_heads;
   int32_t hidden;
+  int32_t* status;             /* optional device word: KIMI_DEVICE_VUP_WAIT when a wait gave up
+                                  (each wait keeps a fixed ~2 s bound); NULL = not reported */
 } KimiVUpOProjParams;
 
 KIMI_API int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* params, void* stream);

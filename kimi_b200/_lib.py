@@ -41,6 +41,8 @@ ABI_VERSION = 201
 DEVICE_WAIT_BITS = 0x1FF
 DEVICE_BAD_PAGE = 0x200
 DEVICE_PEER_WAIT = 0x400
+DEVICE_QABSORB_WAIT = 0x800
+DEVICE_VUP_WAIT = 0x1000
 
 AR_MAX_INPUTS = 8
 
@@ -125,6 +127,7 @@ class KimiQAbsorbParams(ctypes.Structure):
         ("num_heads", ctypes.c_int32),
         ("is_neox", ctypes.c_int32),
         ("legacy_rule", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
     ]
 
 
@@ -179,6 +182,7 @@ class KimiVUpOProjParams(ctypes.Structure):
         ("num_tokens", ctypes.c_int32),
         ("num_heads", ctypes.c_int32),
         ("hidden", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
     ]
 
 

@@ -21,7 +21,8 @@ static_assert(kimi::kStatusSoftmaxWait == KIMI_DEVICE_SOFTMAX_WAIT && kimi::kSta
                   kimi::kStatusIssuerPvWait == KIMI_DEVICE_ISSUER_PV_WAIT &&
                   kimi::kStatusConverterWait == KIMI_DEVICE_CONVERTER_WAIT && kimi::kStatusDrain == KIMI_DEVICE_DRAIN_WAIT &&
                   kimi::kStatusProducerWait == KIMI_DEVICE_PRODUCER_WAIT && kimi::kStatusBadPage == KIMI_DEVICE_BAD_PAGE &&
-                  kimi::kStatusScaleWait == KIMI_DEVICE_SCALE_WAIT && kimi::kStatusPeerWait == KIMI_DEVICE_PEER_WAIT,
+                  kimi::kStatusScaleWait == KIMI_DEVICE_SCALE_WAIT && kimi::kStatusPeerWait == KIMI_DEVICE_PEER_WAIT &&
+                  kimi::kStatusQAbsorbWait == KIMI_DEVICE_QABSORB_WAIT && kimi::kStatusVupWait == KIMI_DEVICE_VUP_WAIT,
               "device status bits of the kernels and the header agree");
 
 inline bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
@@ -424,6 +425,8 @@ int kimi_mla_q_absorb_rope_append(const KimiQAbsorbParams* p, void* stream) {
   a.num_heads = p->num_heads;
   a.is_neox = p->is_neox;
   a.legacy_rule = p->legacy_rule;
+  if (p->status && !aligned(p->status, 4)) return KIMI_ERR_MISALIGNED;
+  a.status = p->status;
   return cuda_status(kimi::launch_q_absorb(a, static_cast<cudaStream_t>(stream)));
 }
 
@@ -523,6 +526,8 @@ int kimi_mla_v_up_o_proj(const KimiVUpOProjParams* p, void* stream) {
   a.num_tokens = p->num_tokens;
   a.num_heads = p->num_heads;
   a.hidden = p->hidden;
+  if (p->status && !aligned(p->status, 4)) return KIMI_ERR_MISALIGNED;
+  a.status = p->status;
   const cuuint64_t T = static_cast<cuuint64_t>(p->num_tokens), H = static_cast<cuuint64_t>(p->num_heads);
   const cuuint64_t K = 128 * H, stride_t = 2 * static_cast<cuuint64_t>(p->o_stride_t);
   // a single head's stride is never used: give it the extent of the tokens
@@ -560,7 +565,7 @@ int kimi_device_status(int32_t* device_word, int32_t clear, void* stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e == cudaSuccess && clear) e = cudaMemsetAsync(device_word, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return cuda_status(e);
-  return host & 0x7FF;
+  return host & 0x1FFF;
 }
 
 int kimi_mxfp4_quantize(const void* x, int64_t rows, int64_t cols, int64_t x_stride, void* nibbles, void* scales,

@@ -40,6 +40,8 @@ enum : int {
   kStatusProducerWait = 256,
   kStatusBadPage = 512,
   kStatusPeerWait = 1024,
+  kStatusQAbsorbWait = 2048,
+  kStatusVupWait = 4096,
   kStatusScaleWait = 8,
 };
 // Default bound of a device wait when the caller passes 0 (2 s).
@@ -85,6 +87,7 @@ struct QAbsorbArgs {
   int num_heads;
   int is_neox;
   int legacy_rule;
+  int* status;  // optional device word (kStatusQAbsorbWait)
 };
 
 // Sum of the ranks' partial rows + residual, RMSNorm, MXFP4 (one CTA per row).
@@ -133,6 +136,7 @@ struct VUpOProjArgs {
   int num_tokens;
   int num_heads;
   int hidden;
+  int* status;  // optional device word (kStatusVupWait)
 };
 
 // TMA maps of the V up-projection + o_proj operands, all bf16 with 128-byte

@@ -261,6 +261,7 @@ __global__ void __launch_bounds__(256, 2) mla_q_absorb_kernel(const __grid_const
   bool done = false;
   for (uint32_t i = 0; i < kPolls && !done; ++i) done = mbar_try_wait_sleep(mbar, 0, kWaitSleepNs);
   done = __all_sync(0xffffffffu, done);  // warp-uniform: the TMEM load below is warp-wide
+  if (!done && lane == 0 && a.status) atomicOr(a.status, kStatusQAbsorbWait);
   fence_after_sync();
   const int q = warp & 3, half = warp >> 2, r = 32 * q + lane;
   if (done) {

@@ -92,6 +92,11 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* mbar, uint32_t parity, v
   return false;
 }
 
+// the caller's status word, once per CTA that gave up
+__device__ __forceinline__ void report_give_up(const VUpOProjArgs& a, volatile int* abort) {
+  if (*abort && a.status && threadIdx.x == 0) atomicOr(a.status, kStatusVupWait);
+}
+
 // fp32 TMEM columns of this thread's lane -> 32 bf16 at dst (64 B)
 __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const uint32_t (&v)[32]) {
   uint4* d = reinterpret_cast<uint4*>(dst);
@@ -174,6 +179,7 @@ __global__ void __launch_bounds__(256, 1)
   }
   fence_before_sync();
   __syncthreads();
+  report_give_up(a, abort);
   if (warp == 0) {
     fence_after_sync();
     tmem_dealloc(tmem, kCols);
@@ -276,6 +282,7 @@ __global__ void __launch_bounds__(256, 1)
   }
   fence_before_sync();
   __syncthreads();
+  report_give_up(a, abort);
   if (warp == 0) {
     fence_after_sync();
     tmem_dealloc(tmem, kP2TmemCols);

@@ -291,7 +291,7 @@ def q_absorb_rope_append(q_nope: torch.Tensor, q_pe: torch.Tensor, w_uk: torch.T
                          k_pe: torch.Tensor, positions: torch.Tensor, cos_cache: torch.Tensor,
                          sin_cache: torch.Tensor, kv_buffer: torch.Tensor, kv_scales: torch.Tensor,
                          slot_mapping: torch.Tensor, q_out: torch.Tensor | None = None, is_neox: bool = False,
-                         legacy_rule: bool = False) -> torch.Tensor:
+                         legacy_rule: bool = False, status: torch.Tensor | None = None) -> torch.Tensor:
     """The decode step before attention in one launch (the reference's
     ``fused_kv_bmm``, patches/atom-optimizations.patch:468-639):
 
@@ -343,14 +343,17 @@ def q_absorb_rope_append(q_nope: torch.Tensor, q_pe: torch.Tensor, w_uk: torch.T
         kv_scales=kv_scales.data_ptr(), num_pages=num_pages, q_out=q_out.data_ptr(),
         q_out_stride_t=q_out.stride(0), q_out_stride_h=q_out.stride(1), num_tokens=T, num_heads=H,
         is_neox=int(bool(is_neox)), legacy_rule=int(bool(legacy_rule)))
+    if status is not None:
+        _require_status_word(status, dev)
+        p.status = status.data_ptr()
     with torch.cuda.device(dev):
-        status = _lib.load().kimi_mla_q_absorb_rope_append(ctypes.byref(p), _stream_handle(dev))
-    _lib.check(status, "kimi_mla_q_absorb_rope_append")
+        st = _lib.load().kimi_mla_q_absorb_rope_append(ctypes.byref(p), _stream_handle(dev))
+    _lib.check(st, "kimi_mla_q_absorb_rope_append")
     return q_out
 
 
 def v_up_proj_and_o_proj(o: torch.Tensor, w_uv: torch.Tensor, w_o: torch.Tensor, out: torch.Tensor | None = None,
-                         x: torch.Tensor | None = None) -> torch.Tensor:
+                         x: torch.Tensor | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
     """The decode step after attention (the reference's
     ``_v_up_proj_and_o_proj(o, heads_first=True)``,
     patches/atom-optimizations.patch:131-143 and :297-302):
@@ -367,7 +370,9 @@ def v_up_proj_and_o_proj(o: torch.Tensor, w_uv: torch.Tensor, w_o: torch.Tensor,
     returned: this rank's partial of the tensor-parallel all-reduce, so it
     may be a :class:`kimi_b200.tp.PeerPartials` ``local`` buffer.  ``x`` is a
     bf16 [T, H * 128] contiguous scratch (allocated when None) that holds the
-    up-projection afterwards.
+    up-projection afterwards.  ``status``: optional int32 [1] device word that
+    gets ``DEVICE_VUP_WAIT`` when a wait gave up (read it with
+    :func:`device_status`).
     """
     dev = _require_cuda(o, w_uv, w_o)
     for name, t in (("o", o), ("w_uv", w_uv), ("w_o", w_o)):
@@ -392,9 +397,12 @@ def v_up_proj_and_o_proj(o: torch.Tensor, w_uv: torch.Tensor, w_o: torch.Tensor,
     p = _lib.KimiVUpOProjParams(o=o.data_ptr(), o_stride_h=o.stride(0), o_stride_t=o.stride(1), w_uv=w_uv.data_ptr(),
                                 w_o=w_o.data_ptr(), x=x.data_ptr(), out=out.data_ptr(), out_stride=out.stride(0),
                                 num_tokens=T, num_heads=H, hidden=hidden)
+    if status is not None:
+        _require_status_word(status, dev)
+        p.status = status.data_ptr()
     with torch.cuda.device(dev):
-        status = _lib.load().kimi_mla_v_up_o_proj(ctypes.byref(p), _stream_handle(dev))
-    _lib.check(status, "kimi_mla_v_up_o_proj")
+        st = _lib.load().kimi_mla_v_up_o_proj(ctypes.byref(p), _stream_handle(dev))
+    _lib.check(st, "kimi_mla_v_up_o_proj")
     return out
 
 

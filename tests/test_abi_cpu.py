@@ -45,6 +45,8 @@ def test_device_status_texts():
     both = _lib.status_text(_lib.DEVICE_BAD_PAGE | 0x040)
     assert "gave up" in both and "outside the cache" in both
     assert "peer rank" in _lib.status_text(_lib.DEVICE_PEER_WAIT)
+    assert "gave up" in _lib.status_text(_lib.DEVICE_QABSORB_WAIT)
+    assert "gave up" in _lib.status_text(_lib.DEVICE_VUP_WAIT)
     # every combination of device bits stays below the CUDA error range
     assert "gave up" in _lib.status_text(0x3FF) and "peer rank" in _lib.status_text(0x7FF)
     assert 0x7FF < _lib.KIMI_ERR_CUDA_BASE
@@ -194,3 +196,33 @@ def test_tp8_entry_points_reject_bad_arguments_on_host():
                                  weight=0x3000, nibbles=0x4000, scales=0x5000)
     p.inputs[0], p.inputs[1] = 0x6000, 0x7008
     assert lib.kimi_ar_rmsnorm_mxfp4(ctypes.byref(p), None) == -4              # misaligned partial
+
+
+def test_ctypes_structs_match_the_header_layout(tmp_path):
+    """Every params struct of _lib has the C header's field offsets and size:
+    a small C program built against include/kimi_mla.h prints them."""
+    import os
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    structs = [name for name in dir(_lib) if name.startswith("Kimi") and name.endswith("Params")]
+    assert structs
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "kimi_mla.h"', "int main(void) {"]
+    for name in structs:
+        lines.append(f'  printf("{name} size %zu\\n", sizeof({name}));')
+        for field, _ in getattr(_lib, name)._fields_:
+            lines.append(f'  printf("{name} {field} %zu\\n", offsetof({name}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run(["gcc", "-I", inc, str(src), "-o", str(exe)], check=True)
+    got = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    c_layout = {tuple(line.split()[:2]): int(line.split()[2]) for line in got if line}
+    for name in structs:
+        st = getattr(_lib, name)
+        assert c_layout[(name, "size")] == ctypes.sizeof(st), name
+        for field, _ in st._fields_:
+            assert c_layout[(name, field)] == getattr(st, field).offset, (name, field)

@@ -47,12 +47,14 @@ def _run(c, is_neox, legacy=False):
     q = _bf16(c["q"])
     kvb = torch.zeros(c["pages"], 64, omla.TOKEN_BYTES, dtype=torch.uint8, device=DEV)
     kvs = torch.zeros(c["pages"], 64, omla.SCALE_BYTES, dtype=torch.uint8, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
     q_out = kimi_b200.q_absorb_rope_append(
         q[:, :, :128], q[:, :, 128:], _bf16(c["w_uk"]), _bf16(c["kv_c"]), _bf16(c["k_pe"]),
         torch.from_numpy(c["positions"]).to(DEV), torch.from_numpy(c["cos"]).to(DEV),
         torch.from_numpy(c["sin"]).to(DEV), kvb, kvs, torch.from_numpy(c["slots"]).to(DEV), is_neox=is_neox,
-        legacy_rule=legacy)
+        legacy_rule=legacy, status=status)
     torch.cuda.synchronize()
+    assert kimi_b200.device_status(status) == 0  # no wait gave up
     return q_out, kvb.cpu().numpy(), kvs.cpu().numpy()
 
 

@@ -64,8 +64,10 @@ def test_matches_oracle(heads, tokens, hidden, pad_heads, pad_tokens):
     x_ref, out_ref = ovu.v_up_o_proj(o_np, w_uv, w_o)
     o = _t(o_full)[:heads, :tokens]  # heads-first view: strides (pad_tokens * 512, 512, 1)
     x = torch.empty(tokens, heads * 128, dtype=torch.bfloat16, device=DEV)
-    out = kimi_b200.v_up_proj_and_o_proj(o, _t(w_uv), _t(w_o), x=x)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = kimi_b200.v_up_proj_and_o_proj(o, _t(w_uv), _t(w_o), x=x, status=status)
     torch.cuda.synchronize()
+    assert kimi_b200.device_status(status) == 0  # no wait gave up
     _check_x(_bits(x), x_ref)
     _check_out(_bits(out), out_ref)
 

@@ -67,11 +67,20 @@ def local_batch(indices: Sequence[int], kv_indptr: torch.Tensor, kv_indices: tor
 
 
 def gather_outputs(o_local: torch.Tensor, shards: Sequence[Sequence[int]], rank: int, world: int,
-                   batch: int, dst: int = 0, group=None) -> torch.Tensor | None:
+                   batch: int, dst: int = 0, group=None, timeout: float | None = None) -> torch.Tensor | None:
     """Outputs of all ranks in batch order on rank ``dst`` (None elsewhere).
 
     ``o_local`` is this rank's ``[len(shards[rank]), heads, 512]`` result in
-    the order of ``shards[rank]``.  Every rank takes part (one all_gather)."""
+    the order of ``shards[rank]``.  Every rank takes part (one all_gather).
+
+    ``timeout`` (seconds): bound of the wait for the other ranks.  A rank that
+    does not join within it (it failed before the gather, or never reached
+    it) makes this call raise ``RuntimeError`` on the ranks that did join,
+    instead of leaving them blocked until the process group's own timeout;
+    the process group is then not to be used again.  ``None`` waits as the
+    process group does."""
+    import datetime
+
     import torch.distributed as dist
 
     if len(shards) != world or o_local.shape[0] != len(shards[rank]):
@@ -85,7 +94,15 @@ def gather_outputs(o_local: torch.Tensor, shards: Sequence[Sequence[int]], rank:
     padded = torch.zeros((rows,) + tail, dtype=o_local.dtype, device=o_local.device)
     padded[: o_local.shape[0]] = o_local
     parts = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(parts, padded.contiguous(), group=group)
+    work = dist.all_gather(parts, padded.contiguous(), group=group, async_op=True)
+    try:
+        if timeout is None:
+            work.wait()
+        else:
+            work.wait(timeout=datetime.timedelta(seconds=timeout))
+    except Exception as e:  # noqa: BLE001 - every backend's timeout or peer-loss error
+        raise RuntimeError(f"gather_outputs: not every rank joined the gather on rank {rank} "
+                           f"({type(e).__name__}: {e})") from e
     if rank != dst:
         return None
     out = torch.empty((batch,) + tail, dtype=o_local.dtype, device=o_local.device)

@@ -80,3 +80,50 @@ def test_two_rank_gather_equals_single_batch(world):
     rng = np.random.default_rng(11)
     lens = [int(x) for x in rng.integers(1, 600, 7)] + [0]
     mp.spawn(_rank_main, args=(world, _free_port(), lens, 11), nprocs=world, join=True)
+
+
+def _failing_rank_main(rank, world, port, result_dir, mode):
+    """Rank 1 fails before the gather: it raises and exits ("exits"), or
+    stays alive without joining ("absent").  Rank 0 must get an error from
+    gather_outputs within its timeout, not block."""
+    import datetime
+    import time
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    done = os.path.join(result_dir, "rank0_done")
+    shards = [[0, 2], [1]]
+    o_local = torch.ones(len(shards[rank]), 4, 512)
+    if rank == 1:
+        if mode == "exits":
+            os._exit(0)  # a rank that died before the gather (no teardown)
+        for _ in range(600):  # alive, never joining, until rank 0 has its answer
+            if os.path.exists(done):
+                break
+            time.sleep(0.05)
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        dp.gather_outputs(o_local, shards, rank, world, batch=3, timeout=2.0)
+        outcome = "returned"
+    except RuntimeError as e:
+        outcome = "raised" if "not every rank joined" in str(e) else f"other: {e}"
+    elapsed = time.monotonic() - t0
+    with open(os.path.join(result_dir, "rank0"), "w") as f:
+        f.write(f"{outcome} {elapsed:.2f}")
+    open(done, "w").close()
+    os._exit(0)  # the group is not to be used again after a failed gather
+
+
+@pytest.mark.parametrize("mode", ["absent", "exits"])
+def test_gather_raises_in_bounded_time_when_a_rank_fails(mode, tmp_path):
+    import torch.multiprocessing as mp
+    ctx = mp.start_processes(_failing_rank_main, args=(2, _free_port(), str(tmp_path), mode), nprocs=2,
+                             join=False, start_method="spawn")
+    for p in ctx.processes:
+        p.join(60)
+        assert p.exitcode == 0, p.exitcode
+    outcome, elapsed = (tmp_path / "rank0").read_text().split()
+    assert outcome == "raised", outcome
+    assert float(elapsed) < 30.0

@@ -9,7 +9,7 @@ library's KV-append quantiser).  A step is one decode call over the whole
 batch (one layer).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload kimi_k2|ragged|long|tp8_prologue|tp8_ar_norm|tp8_vup_oproj]
+                    [--workload kimi_k2|ragged|long|tp8_block|tp8_prologue|tp8_ar_norm|tp8_vup_oproj]
 
 ``--workload ragged`` runs the batch-sharded sweep instead: one batch of 256
 sequences with lengths drawn uniformly from 1K-32K tokens (seeded), spread
@@ -21,6 +21,11 @@ holding only its sequences' pages; the whole batch is fixed as N grows
 128 heads, batch 8, 131072 tokens every sequence, 32 splits into
 preallocated partials, one token appended per sequence per step; it reports
 the HBM fraction and the tensor-pipe fraction of the MMA work.
+
+``--workload tp8_block`` times the whole TP8 decode attention block per GPU
+(config 5): q absorption + RoPE + KV append, the decode (8 heads, 128
+sequences of 4096 tokens), W_UV + o_proj, all-reduce + RMSNorm + MXFP4, as
+one captured chain, in microseconds per layer, with each call's share.
 
 ``--workload tp8_prologue`` times the decode step before attention instead:
 q absorption by W_UK + RoPE + MXFP4 KV append (kimi_b200.q_absorb_rope_append)
@@ -916,6 +921,148 @@ def run_vup(args, rank, world, local_rank):
     }
 
 
+BLK_TOKENS, BLK_HEADS, BLK_CTX, BLK_HIDDEN, BLK_STEPS_PER_GRAPH = 128, 8, 4096, 7168, 8
+BLK_WORKLOAD = (f"Kimi-K2 TP8 decode attention block per GPU: {BLK_TOKENS} decode tokens (one per sequence, "
+                f"ctx {BLK_CTX}), {BLK_HEADS} heads, hidden {BLK_HIDDEN}: q absorption by W_UK + RoPE + KV "
+                f"append, MXFP4 MLA decode (num_kv_splits auto), W_UV + o_proj [1024 -> 7168], all-reduce of "
+                f"the ranks' partials + residual + RMSNorm (eps 1e-6) + MXFP4; weights N(0, 0.02)")
+
+
+def run_block(args, rank, world, local_rank):
+    """The TP8 attention block per GPU as one chain of the library's four
+    calls, captured in a CUDA graph and replayed (the per-call host overhead
+    would otherwise set the pace).  On one GPU, 8 local buffers stand in for
+    the ranks' partials (the one-shot kernel reads them all); under torchrun
+    each rank's real partial is exchanged over NVLink with the two-shot call
+    (its barriers are on the device, so the whole chain captures)."""
+    import torch
+    import torch.distributed as dist
+
+    import kimi_b200 as kimi
+    from kimi_b200 import tp
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T, H, C, D = BLK_TOKENS, BLK_HEADS, BLK_CTX, BLK_HIDDEN
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(23 + 1000 * rank)
+    freqs = 1.0 / (10000.0 ** (torch.arange(32, device=dev, dtype=torch.float64) / 32.0))
+    ang = torch.arange(C, device=dev, dtype=torch.float64)[:, None] * freqs[None, :]
+    cos, sin = ang.cos().float().contiguous(), ang.sin().float().contiguous()
+    pages = T * C // PAGE
+    kvb, kvs = kimi.alloc_mxfp4_cache(pages, dev, zero=False)
+    for start in range(0, pages * PAGE, 1 << 16):
+        n = min(1 << 16, pages * PAGE - start)
+        kimi.mxfp4_kv_append(torch.randn(n, 512, generator=g, device=dev).to(bf),
+                             torch.randn(n, 64, generator=g, device=dev).to(bf), kvb, kvs,
+                             torch.arange(start, start + n, device=dev))
+    perm = torch.randperm(pages, generator=g, device=dev).to(torch.int32)
+    indptr = (torch.arange(T + 1, device=dev, dtype=torch.int32) * (C // PAGE)).contiguous()
+    last = torch.full((T,), PAGE, dtype=torch.int32, device=dev)
+    slots = (perm[indptr[1:].long() - 1].long() * PAGE + (PAGE - 1)).contiguous()  # each sequence's newest token
+    positions = torch.full((T,), C - 1, dtype=torch.int64, device=dev)
+    q = torch.randn(T, H, 192, generator=g, device=dev).to(bf)
+    w_uk = (torch.randn(H, 128, 512, generator=g, device=dev) * 0.02).to(bf)
+    w_uv = (torch.randn(H, 512, 128, generator=g, device=dev) * 0.02).to(bf)
+    w_o = (torch.randn(D, H * 128, generator=g, device=dev) * 0.02).to(bf)
+    kv_c = torch.randn(T, 512, generator=g, device=dev).to(bf)
+    k_pe = torch.randn(T, 64, generator=g, device=dev).to(bf)
+    residual = torch.randn(T, D, generator=g, device=dev).to(bf)
+    norm_w = torch.randn(D, generator=g, device=dev).to(bf)
+    q_out = torch.empty(T, H, 576, dtype=bf, device=dev)
+    o_hf = torch.empty(H, T, 512, dtype=bf, device=dev)
+    x = torch.empty(T, H * 128, dtype=bf, device=dev)
+    ws = kimi.alloc_workspace(T, H, None, dev)
+    if world > 1:
+        peers = tp.PeerPartials(T, D, dev)
+        partial = peers.local
+    else:
+        partial = torch.empty(T, D, dtype=bf, device=dev)
+        others = [torch.randn(T, D, generator=g, device=dev).to(bf) for _ in range(7)]
+        res_out = torch.empty_like(residual)
+        nib = torch.empty(T, D // 2, dtype=torch.uint8, device=dev)
+        sc = torch.empty(T, D // 32, dtype=torch.uint8, device=dev)
+
+    def prologue():
+        kimi.q_absorb_rope_append(q[:, :, :128], q[:, :, 128:], w_uk, kv_c, k_pe, positions, cos, sin, kvb, kvs,
+                                  slots, q_out=q_out)
+
+    def decode():
+        kimi.mla_decode_fwd(q_out, kvb, kvs, o_hf.permute(1, 0, 2), None, indptr, perm, last, sm_scale=SM_SCALE,
+                            workspace=ws)
+
+    def epilogue():
+        kimi.v_up_proj_and_o_proj(o_hf, w_uv, w_o, out=partial, x=x)
+
+    def allreduce():
+        if world > 1:
+            peers.reduce_norm_quant_two_shot(residual, norm_w, 1e-6)
+        else:
+            tp.ar_rmsnorm_mxfp4([partial] + others, residual, norm_w, 1e-6, residual_out=res_out, nibbles=nib,
+                                scales=sc)
+
+    def block():
+        prologue()
+        decode()
+        epilogue()
+        allreduce()
+
+    stream = torch.cuda.current_stream(dev)
+
+    def graph_us(fn, reps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(BLK_STEPS_PER_GRAPH):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * BLK_STEPS_PER_GRAPH)
+        del graph
+        if world > 1:
+            t = torch.tensor([us], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        return us
+
+    reps = max(1, args.steps // BLK_STEPS_PER_GRAPH)
+    with ClockSampler(dev.index) as clocks:
+        us_block = graph_us(block, reps)
+        parts = {name: round(graph_us(fn, reps), 2) for name, fn in
+                 (("prologue", prologue), ("decode", decode), ("v_up_o_proj", epilogue), ("allreduce_norm_quant", allreduce))}
+    status = 0
+    if world > 1:
+        status = kimi.device_status(peers.status)
+        peers.close()
+    if rank != 0:
+        return None
+    return {
+        "metric": "TP8 decode attention block µs/layer per GPU (Kimi-K2, 128 tokens, ctx 4096, hidden 7168)",
+        "value": round(us_block, 2), "unit": "us", "n_gpus": world, "steps": reps * BLK_STEPS_PER_GRAPH,
+        "warmup": args.warmup, "ms_per_step": round(us_block / 1e3, 5), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded normal activations, N(0, 0.02) weights, cache written by the library's MXFP4 "
+                "KV-append)",
+        "config": {"workload": BLK_WORKLOAD, "tokens": T, "heads_per_gpu": H, "ctx": C, "hidden": D,
+                   "allreduce": ("two-shot over NVLink, device barriers" if world > 1 else
+                                 "one-shot over 8 local buffers standing in for the ranks' partials"),
+                   "parallelism": f"tp{world}" if world > 1 else "tp8 block on one GPU (8 stand-in partials)",
+                   "graph": f"{BLK_STEPS_PER_GRAPH} blocks per captured graph, {reps} replays"},
+        "parts_us": parts, "gpu_launches": reps * BLK_STEPS_PER_GRAPH * 8,
+        "peer_status": status, "clocks": clocks.summary(),
+    }
+
+
 LONG_HEADS, LONG_BATCH, LONG_CTX, LONG_SPLITS = 128, 8, 131072, 32
 LONG_WORKLOAD = (f"DeepSeek-V3-shape MXFP4 MLA decode, long context: {LONG_HEADS} heads, batch {LONG_BATCH}, "
                  f"ctx {LONG_CTX} every sequence, page {PAGE}, seeded random-permutation page table, "
@@ -1044,7 +1191,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "long", "tp8_prologue", "tp8_ar_norm", "tp8_vup_oproj"],
+    ap.add_argument("--workload", choices=["kimi_k2", "ragged", "long", "tp8_block", "tp8_prologue", "tp8_ar_norm",
+                                                "tp8_vup_oproj"],
                     default="kimi_k2")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
                     help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
@@ -1070,7 +1218,7 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         runner = {"tp8_prologue": run_prologue, "tp8_ar_norm": run_ar_norm, "tp8_vup_oproj": run_vup,
-                  "long": run_long}.get(args.workload, run_ours)
+                  "long": run_long, "tp8_block": run_block}.get(args.workload, run_ours)
         line = runner(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)

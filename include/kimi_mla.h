@@ -316,8 +316,8 @@ KIMI_API int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* params, void* stre
 
 /* The same step as a two-shot exchange over peer memory, with its own device
  * barriers (the same reference interface as kimi_ar_rmsnorm_mxfp4).  Every
- * rank of `world` calls it with the same rows, hidden, eps, weight values and
- * epoch; rank r computes rows [r rows / world, (r + 1) rows / world) from all
+ * rank of `world` calls it with the same rows, hidden, eps and weight values;
+ * rank r computes rows [r rows / world, (r + 1) rows / world) from all
  * ranks' partials and stores those rows' residual_out, nibbles and scales into
  * every rank's buffers, so that when the call completes each rank holds all
  * rows.  The call waits on the device for the other ranks twice (at entry, so
@@ -330,16 +330,18 @@ KIMI_API int kimi_ar_rmsnorm_mxfp4(const KimiArRmsNormParams* params, void* stre
  * GPU can read and write (its own buffers and peer buffers mapped over
  * NVLink, for example with CUDA IPC).  flags: every rank's int32
  * [2 * KIMI_AR_MAX_INPUTS], zero before the first call; counter: this rank's
- * int32, zero before the first call (each call leaves it zero); epoch: 1 for
- * the first call, then one more for each call (the same on every rank).  No
- * TMA or bulk copy touches peer memory: plain loads and stores only. */
+ * int32 [2], zero before the first call: [0] counts the call's CTAs (each call
+ * leaves it zero), [1] numbers the calls (each call reads it, uses the next
+ * number as the barriers' epoch and leaves it there), so a call captured in a
+ * CUDA graph may be replayed.  Every rank makes the same sequence of calls.
+ * No TMA or bulk copy touches peer memory: plain loads and stores only. */
 typedef struct KimiArTwoShotParams {
   const void* inputs[KIMI_AR_MAX_INPUTS];  /* every rank's partial, bf16 [rows, hidden] */
   void* residual_out[KIMI_AR_MAX_INPUTS];  /* every rank's bf16 [rows, hidden] */
   void* nibbles[KIMI_AR_MAX_INPUTS];       /* every rank's uint8 [rows, hidden / 2] */
   void* scales[KIMI_AR_MAX_INPUTS];        /* every rank's uint8 [rows, hidden / 32] */
   int32_t* flags[KIMI_AR_MAX_INPUTS];      /* every rank's int32 [2 * KIMI_AR_MAX_INPUTS] */
-  int32_t* counter;                        /* this rank's int32 */
+  int32_t* counter;                        /* this rank's int32 [2] (CTA count, call number) */
   const void* residual;                    /* this rank's bf16 [rows, hidden] (equal on every rank) */
   const void* weight;                      /* bf16 [hidden] */
   float eps;
@@ -348,7 +350,6 @@ typedef struct KimiArTwoShotParams {
   int32_t legacy_rule;
   int32_t world;                           /* 1 .. KIMI_AR_MAX_INPUTS */
   int32_t rank;
-  int32_t epoch;
   int32_t* status;                         /* optional device word (KIMI_DEVICE_PEER_WAIT) */
   uint64_t timeout_ns;
 } KimiArTwoShotParams;

@@ -163,7 +163,6 @@ class KimiArTwoShotParams(ctypes.Structure):
         ("legacy_rule", ctypes.c_int32),
         ("world", ctypes.c_int32),
         ("rank", ctypes.c_int32),
-        ("epoch", ctypes.c_int32),
         ("status", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_uint64),
     ]

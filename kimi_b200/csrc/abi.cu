@@ -497,7 +497,6 @@ int kimi_ar_rmsnorm_mxfp4_two_shot(const KimiArTwoShotParams* p, void* stream) {
   t.timeout_ns = p->timeout_ns ? p->timeout_ns : kimi::kDefaultTimeoutNs;
   t.world = p->world;
   t.rank = p->rank;
-  t.epoch = p->epoch;
   // zero rows still take part in both barriers (every rank makes the same calls)
   return cuda_status(kimi::launch_ar_two_shot(t, static_cast<cudaStream_t>(stream)));
 }

@@ -209,8 +209,11 @@ __global__ void __launch_bounds__(256) ar_norm_quant_kernel(const __grid_constan
 // rank reading all N partials whole.
 //
 // Two flag barriers over the ranks' flag words (int32 [2][N] per rank, slot
-// [phase][source rank]; a rank writes the call's epoch into every rank's
-// slot, and waits until its own N slots of the phase hold it):
+// [phase][source rank]; a rank writes the call's epoch -- its own call
+// counter (counter[1]) plus one, the same on every rank since all make the
+// same calls -- into every rank's slot, and waits until its own N slots of
+// the phase hold it; the counter lives on the device, so a captured call
+// replays correctly):
 //   * entry: a rank's partial is complete when its call starts (stream
 //     order); nobody reads a partial before all N ranks have entered;
 //   * exit: the last CTA of a rank to finish its rows (a counter in the
@@ -244,23 +247,23 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Thread 0 (after a CTA barrier): this rank's slot of `phase` in every rank's
 // flag words := the epoch.
-__device__ __forceinline__ void signal_all_ranks(const ArTwoShotArgs& t, int phase) {
+__device__ __forceinline__ void signal_all_ranks(const ArTwoShotArgs& t, int phase, int epoch) {
   fence_acq_rel_sys();
-  for (int r = 0; r < t.world; ++r) st_relaxed_sys(t.flags[r] + phase * kArMaxInputs + t.rank, t.epoch);
+  for (int r = 0; r < t.world; ++r) st_relaxed_sys(t.flags[r] + phase * kArMaxInputs + t.rank, epoch);
 }
 
 // Threads 0 .. world - 1 each wait for one rank's slot of `phase` to reach
 // the epoch (epochs are compared as the difference, so they may wrap); the
 // CTA's verdict is the AND over them.
-__device__ __forceinline__ bool wait_all_ranks(const ArTwoShotArgs& t, int phase) {
+__device__ __forceinline__ bool wait_all_ranks(const ArTwoShotArgs& t, int phase, int epoch) {
   __shared__ int failed;
   if (threadIdx.x == 0) failed = 0;
   __syncthreads();
   if (static_cast<int>(threadIdx.x) < t.world) {
     const int* slot = t.flags[t.rank] + phase * kArMaxInputs + threadIdx.x;
-    if (ld_relaxed_sys(slot) - t.epoch < 0) {
+    if (ld_relaxed_sys(slot) - epoch < 0) {
       const uint64_t t0 = global_ns();
-      while (ld_relaxed_sys(slot) - t.epoch < 0) {
+      while (ld_relaxed_sys(slot) - epoch < 0) {
         if (global_ns() - t0 >= t.timeout_ns) {
           atomicExch(&failed, 1);
           break;
@@ -283,8 +286,11 @@ __global__ void __launch_bounds__(256) ar_two_shot_kernel(const __grid_constant_
   // entry: CTA 0 announces this rank (its partial is complete: stream order),
   // every CTA waits for all ranks.  A CTA whose wait gave up skips its row but
   // still counts itself below, so the counter stays in step.
-  if (blockIdx.x == 0 && threadIdx.x == 0) signal_all_ranks(t, 0);
-  const bool entered = wait_all_ranks(t, 0);
+  // the call's number: one past the previous call's (the counter word is
+  // advanced by this call's last CTA, after every CTA has read it here)
+  const int epoch = *reinterpret_cast<volatile int*>(t.counter + 1) + 1;
+  if (blockIdx.x == 0 && threadIdx.x == 0) signal_all_ranks(t, 0, epoch);
+  const bool entered = wait_all_ranks(t, 0, epoch);
   const int row = begin + static_cast<int>(blockIdx.x);
   if (entered && row < end) {
     RowDest d;
@@ -306,12 +312,13 @@ __global__ void __launch_bounds__(256) ar_two_shot_kernel(const __grid_constant_
     asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(done) : "l"(t.counter) : "memory");
     last = done == static_cast<int>(gridDim.x) - 1;
     if (last) {
-      *t.counter = 0;  // the next call is stream-ordered after this one
-      signal_all_ranks(t, 1);
+      t.counter[0] = 0;      // the next call is stream-ordered after this one
+      t.counter[1] = epoch;  // every CTA of this call has read the previous number
+      signal_all_ranks(t, 1, epoch);
     }
   }
   __syncthreads();
-  if (last) wait_all_ranks(t, 1);
+  if (last) wait_all_ranks(t, 1, epoch);
 }
 
 }  // namespace

@@ -116,12 +116,11 @@ struct ArTwoShotArgs {
   uint8_t* nibbles[kArMaxInputs];             // every rank's [rows, hidden / 2]
   uint8_t* scales[kArMaxInputs];              // every rank's [rows, hidden / 32]
   int* flags[kArMaxInputs];                   // every rank's flag words [2][kArMaxInputs]
-  int* counter;                               // this rank's CTA counter (0 between calls)
+  int* counter;                               // this rank's [CTA count (0 between calls), call number]
   int* status;                                // optional device word (kStatusPeerWait)
   unsigned long long timeout_ns;              // bound of each barrier wait
   int world;
   int rank;
-  int epoch;                                  // the call's number, the same on every rank
 };
 
 struct VUpOProjArgs {

@@ -180,10 +180,10 @@ class PeerPartials:
         self.residual_out = self._region("residual_out", torch.bfloat16, (rows, hidden))
         self.nibbles = self._region("nibbles", torch.uint8, (rows, hidden // 2))
         self.scales = self._region("scales", torch.uint8, (rows, hidden // 32))
-        # this rank's CTA counter and device status word (not shared)
+        # this rank's two-shot counter words (CTA count, call number) and its
+        # device status word (not shared)
         self._words = torch.zeros(4, dtype=torch.int32, device=self.device)
-        self.status = self._words[1:2]
-        self.epoch = 0
+        self.status = self._words[2:3]
         ptr = self.buffer.data_ptr()
         # Every rank joins the gather even when its export failed (an
         # allocation from PYTORCH_CUDA_ALLOC_CONF=expandable_segments has no
@@ -277,7 +277,9 @@ class PeerPartials:
         1 / N of the rows from every partial and stores them into every rank's
         outputs, the ranks meeting at two device barriers (no host barrier).
         Collective: every rank calls it, in the same order, with the same
-        shapes.  Returns views of this rank's outputs ``(residual_out [rows,
+        shapes (the call numbers that pair the ranks' barriers live on the
+        device, so the call may be captured in a CUDA graph and replayed).
+        Returns views of this rank's outputs ``(residual_out [rows,
         hidden], nibbles [rows, hidden/2], scales [rows, hidden/32])``, valid
         until the next call.  A barrier wait that runs out (``timeout_ns``, 0 =
         2 s) sets ``_lib.DEVICE_PEER_WAIT`` in ``self.status`` (read it with
@@ -292,7 +294,6 @@ class PeerPartials:
             raise ValueError("weight must be a contiguous bf16 [hidden] tensor")
         if not self.bases:
             raise RuntimeError("PeerPartials is closed")
-        self.epoch += 1
         p = _lib.KimiArTwoShotParams()
         for r, base in enumerate(self.bases):
             p.inputs[r] = base + self._off["partial"]
@@ -304,7 +305,7 @@ class PeerPartials:
         p.residual, p.weight = residual.data_ptr(), weight.data_ptr()
         p.eps = float(eps)
         p.rows, p.hidden, p.legacy_rule = rows, self.hidden, int(bool(legacy_rule))
-        p.world, p.rank, p.epoch = self.world, self.rank, self.epoch
+        p.world, p.rank = self.world, self.rank
         p.status = self.status.data_ptr()
         p.timeout_ns = int(timeout_ns)
         with torch.cuda.device(self.device):

@@ -82,7 +82,7 @@ def test_residual_updated_in_place():
 # ---------------------------------------------------------------------------
 # two-shot form (kimi_ar_rmsnorm_mxfp4_two_shot)
 # ---------------------------------------------------------------------------
-def _two_shot_params(world, rank, parts, outs, flags, counter, res, w, rows, hidden, epoch, status=None,
+def _two_shot_params(world, rank, parts, outs, flags, counter, res, w, rows, hidden, status=None,
                      timeout_ns=0):
     from kimi_b200 import _lib
     p = _lib.KimiArTwoShotParams()
@@ -93,7 +93,7 @@ def _two_shot_params(world, rank, parts, outs, flags, counter, res, w, rows, hid
     p.counter = counter.data_ptr()
     p.residual, p.weight = res.data_ptr(), w.data_ptr()
     p.eps, p.rows, p.hidden, p.legacy_rule = 1e-6, rows, hidden, 0
-    p.world, p.rank, p.epoch = world, rank, epoch
+    p.world, p.rank = world, rank
     p.status = status.data_ptr() if status is not None else None
     p.timeout_ns = timeout_ns
     return p
@@ -106,21 +106,23 @@ def _outs(rows, hidden, dev=DEV):
 
 
 def test_two_shot_one_rank_matches_oracle_over_several_epochs():
-    """One rank: both barriers meet at once; three calls (epochs 1..3) on new
-    inputs, each bit-exact against the oracle, the counter left at zero."""
+    """One rank: both barriers meet at once; three calls (epochs 1..3, kept
+    on the device) on new inputs, each bit-exact against the oracle; the CTA
+    counter is left at zero and the call counter at 3.  Then a captured call
+    replayed twice takes epochs 4 and 5."""
     import ctypes
     from kimi_b200 import _lib
     lib = _lib.load()
     rows, hidden = 37, 7168
     flags = [torch.zeros(16, dtype=torch.int32, device=DEV)]
-    counter = torch.zeros(1, dtype=torch.int32, device=DEV)
+    counter = torch.zeros(2, dtype=torch.int32, device=DEV)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     outs = [_outs(rows, hidden)]
     for epoch in (1, 2, 3):
         rng = np.random.default_rng(90 + epoch)
         x, res, w = _bf16_np(rng, (rows, hidden)), _bf16_np(rng, (rows, hidden)), _bf16_np(rng, (hidden,))
         part, rt, wt = _t(x), _t(res), _t(w)
-        p = _two_shot_params(1, 0, [part], outs, flags, counter, rt, wt, rows, hidden, epoch, status)
+        p = _two_shot_params(1, 0, [part], outs, flags, counter, rt, wt, rows, hidden, status)
         st = lib.kimi_ar_rmsnorm_mxfp4_two_shot(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
         assert st == 0, _lib.status_text(st)
         torch.cuda.synchronize()
@@ -128,8 +130,16 @@ def test_two_shot_one_rank_matches_oracle_over_several_epochs():
         np.testing.assert_array_equal(_bits(outs[0][0]), comb)
         np.testing.assert_array_equal(outs[0][1].cpu().numpy(), nib)
         np.testing.assert_array_equal(outs[0][2].cpu().numpy(), sc)
-    assert counter.item() == 0 and status.item() == 0
+    assert counter.cpu().tolist() == [0, 3] and status.item() == 0
     assert flags[0].cpu().tolist()[:1] == [3] and flags[0].cpu().tolist()[8:9] == [3]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        lib.kimi_ar_rmsnorm_mxfp4_two_shot(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(_bits(outs[0][0]), comb)
+    assert counter.cpu().tolist() == [0, 5] and flags[0].cpu().tolist()[8:9] == [5] and status.item() == 0
 
 
 def test_two_shot_missing_rank_runs_out_and_reports():
@@ -144,23 +154,23 @@ def test_two_shot_missing_rank_runs_out_and_reports():
     parts = [torch.zeros(rows, hidden, dtype=torch.bfloat16, device=DEV) for _ in range(2)]
     outs = [_outs(rows, hidden) for _ in range(2)]
     flags = [torch.zeros(16, dtype=torch.int32, device=DEV) for _ in range(2)]
-    counter = torch.zeros(1, dtype=torch.int32, device=DEV)
+    counter = torch.zeros(2, dtype=torch.int32, device=DEV)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     res = torch.ones(rows, hidden, dtype=torch.bfloat16, device=DEV)
     w = torch.ones(hidden, dtype=torch.bfloat16, device=DEV)
-    p = _two_shot_params(2, 0, parts, outs, flags, counter, res, w, rows, hidden, 1, status, timeout_ns=200_000)
+    p = _two_shot_params(2, 0, parts, outs, flags, counter, res, w, rows, hidden, status, timeout_ns=200_000)
     st = lib.kimi_ar_rmsnorm_mxfp4_two_shot(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
     assert st == 0
     bits = kimi_b200.device_status(status)
     assert bits == _lib.DEVICE_PEER_WAIT, hex(bits)
     assert torch.count_nonzero(outs[0][0]).item() == 0  # nothing was computed
-    assert counter.item() == 0
+    assert counter.cpu().tolist() == [0, 1]
     torch.ones(4, device=DEV).sum().item()  # the context still works
 
 
 def _ranks_worker(rank, world, port, result_dir):
     """Both forms on `world` GPUs, [128, 7168]: bit-exact against the oracle
-    for three different inputs (two-shot epochs 1..3), then each form timed
+    for three different inputs (two-shot calls 1..3), then each form timed
     with CUDA events over 50 calls replayed from a CUDA graph (the two-shot
     call with its device barriers; the one-shot kernel without the host
     barriers it needs) -- written to the result file."""
@@ -199,7 +209,7 @@ def _ranks_worker(rank, world, port, result_dir):
         # timing: 50 calls captured in a CUDA graph (the two-shot call, whose
         # barriers are on the device, and the one-shot kernel alone) and
         # replayed once on every rank together, so the host's launch rate
-        # does not enter; the captured two-shot calls carry the next 50 epochs
+        # does not enter (the two-shot call numbers itself on the device)
         for name, fn in (("two_shot_us", lambda: peers.reduce_norm_quant_two_shot(rt, wt, 1e-6)),
                          ("one_shot_kernel_us", lambda: tp.ar_rmsnorm_mxfp4(peers.ptrs, rt, wt, 1e-6))):
             g = torch.cuda.CUDAGraph()

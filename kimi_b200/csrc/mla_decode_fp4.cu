@@ -80,10 +80,10 @@ constexpr uint32_t kPollLimit = 100000;  // polls of up to kWaitSleepNs each: ab
 constexpr int kPrefetchTiles = 4;        // L2 prefetch distance beyond the TMA loads
 
 // Register budgets: 640 threads launch with 96 registers each (61440); the
-// softmax warpgroups take 128, the loaders give back down to 80, the
+// softmax warpgroups take 144, the loaders give back down to 64, the
 // issuer/producer warpgroup to 56.
 constexpr uint32_t kLaunchRegs = 96;
-constexpr uint32_t kSoftmaxRegs = 128, kLoaderRegs = 80, kIssuerRegs = 56;
+constexpr uint32_t kSoftmaxRegs = 144, kLoaderRegs = 64, kIssuerRegs = 56;
 static_assert(kSoftmaxThreads * kSoftmaxRegs + kLoaderThreads * kLoaderRegs + 128 * kIssuerRegs <=
                   kThreads * kLaunchRegs,
               "register split");

@@ -1185,6 +1185,47 @@ def run_long(args, rank, world, local_rank):
     }
 
 
+def run_launches(args, rank, world, local_rank):
+    """Profiler case: build the workload's inputs and make `--launches` stage-1
+    calls (Q prep + decode, no merge), untimed, then print one line.  The
+    captures under `profiles/` run this form (`kimi_k2`: the default Kimi-K2
+    batch; `long`: the 128-head, 8 x 131072 cache with 32 splits)."""
+    import torch
+
+    import kimi_b200 as kimi
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if args.workload == "long":
+        gen = torch.Generator(device=dev).manual_seed(17 + rank)
+        b, h, c, splits = LONG_BATCH, LONG_HEADS, LONG_CTX, LONG_SPLITS
+        pages = b * c // PAGE
+        kvb, kvs = kimi.alloc_mxfp4_cache(pages, dev, zero=False)
+        for start in range(0, pages * PAGE, 1 << 16):
+            n = min(1 << 16, pages * PAGE - start)
+            kimi.mxfp4_kv_append(torch.randn(n, 512, generator=gen, device=dev).to(torch.bfloat16),
+                                 torch.randn(n, 64, generator=gen, device=dev).to(torch.bfloat16), kvb, kvs,
+                                 torch.arange(start, start + n, device=dev))
+        perm = torch.randperm(pages, generator=gen, device=dev).to(torch.int32)
+        indptr = (torch.arange(b + 1, device=dev, dtype=torch.int32) * (c // PAGE)).contiguous()
+        last = torch.full((b,), PAGE, dtype=torch.int32, device=dev)
+        q = torch.randn(b, h, 576, generator=gen, device=dev).to(torch.bfloat16)
+        o = torch.empty(b, h, 512, dtype=torch.bfloat16, device=dev)
+        ws = kimi.alloc_workspace(b, h, splits, dev)
+    elif args.workload == "kimi_k2":
+        wl = build_workload(torch, kimi, dev, seed=1)
+        q, kvb, kvs, o, indptr, perm, last, ws = (wl[k] for k in ("q", "kvb", "kvs", "o", "indptr", "perm", "last", "ws"))
+        splits = None
+    else:
+        raise SystemExit("--launches takes --workload kimi_k2 or long")
+    for _ in range(args.launches):
+        kimi.mla_decode_partial(q, kvb, kvs, o, None, indptr, perm, last, sm_scale=SM_SCALE, num_kv_splits=splits,
+                                workspace=ws)
+    torch.cuda.synchronize()
+    print(f"{args.launches} stage-1 launches of {args.workload}: done", flush=True)
+    return None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1196,6 +1237,8 @@ def main():
                     default="kimi_k2")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0,
                     help="host seconds spent timing the CPU oracle for cpu_baseline (0: omit it)")
+    ap.add_argument("--launches", type=int, default=0,
+                    help="profiler case: make this many untimed stage-1 calls of the workload and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -1219,6 +1262,8 @@ def main():
     try:
         runner = {"tp8_prologue": run_prologue, "tp8_ar_norm": run_ar_norm, "tp8_vup_oproj": run_vup,
                   "long": run_long, "tp8_block": run_block}.get(args.workload, run_ours)
+        if args.launches > 0:
+            runner = run_launches
         line = runner(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)

@@ -268,7 +268,10 @@ __device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArg
     // stage s (and scale slot (j + 2) % 4) were last used by tile j - 2
     if (j >= 2) {
       const uint32_t par = static_cast<uint32_t>(((j - 2) >> 1) & 1);
-      if (!wait_phase(&ms.mb_qkdone[s], par, ms, a, 256) || !wait_phase(&ms.mb_nibread[s], par, ms, a, 256)) break;
+      bool ok = true;  // (both waits through one copy of the wait code)
+#pragma unroll 1
+      for (int w = 0; w < 2 && ok; ++w) ok = wait_phase(w == 0 ? &ms.mb_qkdone[s] : &ms.mb_nibread[s], par, ms, a, 256);
+      if (!ok) break;
     }
     int y[2];
     tile_rows(a, cur, y, true);
@@ -321,17 +324,31 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
   for (int j = 0; j < sc.count; ++j, cursor_next(a, cur)) {
     const int s = j & 1;
     const uint32_t use = static_cast<uint32_t>((j >> 1) & 1);
-    // QK(j) needs the tile's nibbles/scales, its k_pe and A scale factors, S(j-1)
-    // read out of TMEM (single S buffer), and at a piece start that sequence's Q.
-    if (!warp_wait(&ms.mb_rawfull[s], use, ms, a, 16, lane) ||
-        !warp_wait(&ms.mb_kpefull, static_cast<uint32_t>(j & 1), ms, a, 16, lane) ||
-        !warp_wait(&ms.mb_sfafull[s], use, ms, a, 16, lane))
-      break;
-    if (j > 0 && !warp_wait(&ms.mb_sfree, static_cast<uint32_t>((j - 1) & 1), ms, a, 16, lane)) break;
-    if (cursor_first(cur)) {
-      if (!warp_wait(&ms.mb_qready, static_cast<uint32_t>(pieces & 1), ms, a, 16, lane)) break;
-      if (a.q_img && !warp_wait(&ms.mb_qload, static_cast<uint32_t>(pieces & 1), ms, a, 16, lane)) break;
-      ++pieces;
+    // QK(j) needs S(j-1) read out of TMEM (single S buffer), the tile's
+    // nibbles/scales, its k_pe and A scale factors, and at a piece start that
+    // sequence's Q.  The waits go through one copy of the wait code: the
+    // kernel is bound by instruction fetch, and each inlined wait adds its
+    // bounded slow path to the code every sub-partition runs.
+    {
+      const bool first = cursor_first(cur);
+      const int nw = first ? (a.q_img ? 6 : 5) : 4;
+      bool ok = true;
+#pragma unroll 1
+      for (int w = (j > 0 ? 0 : 1); w < nw && ok; ++w) {
+        uint64_t* mb;
+        uint32_t par;
+        switch (w) {
+          case 0: mb = &ms.mb_sfree; par = static_cast<uint32_t>((j - 1) & 1); break;
+          case 1: mb = &ms.mb_rawfull[s]; par = use; break;
+          case 2: mb = &ms.mb_kpefull; par = static_cast<uint32_t>(j & 1); break;
+          case 3: mb = &ms.mb_sfafull[s]; par = use; break;
+          case 4: mb = &ms.mb_qready; par = static_cast<uint32_t>(pieces & 1); break;
+          default: mb = &ms.mb_qload; par = static_cast<uint32_t>(pieces & 1); break;
+        }
+        ok = warp_wait(mb, par, ms, a, 16, lane);
+      }
+      if (!ok) break;
+      if (first) ++pieces;
     }
     fence_after_sync();
     if (lane == 0) {
@@ -345,7 +362,7 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
       // and starts the columns of terms 1 and 2
       const uint32_t sA = smem_addr(sm + kOffNib + s * kNibStage);
       const uint32_t sfa0 = tmem + kColSfa + 16 * s, sfb0 = tmem + kColSfb;
-#pragma unroll
+#pragma unroll 1
       for (int k = 0; k < 8; ++k) {
         const uint32_t koff = (k & 3) * 32;
         const uint32_t byte = 2 * (k & 1);
@@ -620,10 +637,11 @@ __device__ __forceinline__ void store_q_scales(uint32_t tmem, const uint8_t* sf,
 // Q operands of a new piece's sequence (softmax threads).  With Q images in
 // the workspace: one bulk copy of the terms and q_pe (completing mb_qload)
 // and the scale factors from global memory; otherwise quantised here.
+template <bool kQImg>
 __device__ void build_q(uint8_t* sm, Misc& ms, uint32_t tmem, const DecodeArgs& a, int b, int head_base,
                         int heads_here, int warp, int lane) {
   const int tid = threadIdx.x;
-  if (a.q_img) {
+  if constexpr (kQImg) {
     const uint8_t* img = a.q_img + (static_cast<int64_t>(b) * head_blocks(a) + head_block(a)) * kQImageBytes;
     asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the Q prep grid is complete (no-op later)
     if (tid == 0) {
@@ -632,18 +650,19 @@ __device__ void build_q(uint8_t* sm, Misc& ms, uint32_t tmem, const DecodeArgs& 
     }
     if (tid < kNH) ms.R[tid] = 0.f;
     if (warp < 4) store_q_scales(tmem, img + kQTermBytes + kQPeBytes, true, warp, lane);
-    return;
+  } else {
+    uint8_t* sf_stage = sm + kOffP;  // [192 rows][16] e8m0 (P'' is free at a piece start)
+    q_operands(a, b, head_base, heads_here, tid, sm + kOffQ, sm + kOffQpe, sf_stage);
+    if ((tid & 3) == 0) ms.R[tid >> 2] = 0.f;
+    named_bar(kBarSoftmax, kSoftmaxThreads);  // the scale bytes are staged
+    if (warp < 4) store_q_scales(tmem, sf_stage, false, warp, lane);
   }
-  uint8_t* sf_stage = sm + kOffP;  // [192 rows][16] e8m0 (P'' is free at a piece start)
-  q_operands(a, b, head_base, heads_here, tid, sm + kOffQ, sm + kOffQpe, sf_stage);
-  if ((tid & 3) == 0) ms.R[tid >> 2] = 0.f;
-  named_bar(kBarSoftmax, kSoftmaxThreads);  // the scale bytes are staged
-  if (warp < 4) store_q_scales(tmem, sf_stage, false, warp, lane);
 }
 
 // ---------------------------------------------------------------------------
 // Softmax warps (0..7) and the per-piece epilogue
 // ---------------------------------------------------------------------------
+template <bool kQImg>
 __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int head_base, int heads_here,
                         int warp, int lane, float c_log2, const DecodeArgs& a) {
   const int tid = threadIdx.x;
@@ -665,7 +684,7 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     if (first) {
       // a new sequence: its Q replaces the previous one (whose last QK is
       // complete: its S was read; its last PV too: the epilogue waited for it)
-      build_q(sm, ms, tmem, a, cur.b, head_base, heads_here, warp, lane);
+      build_q<kQImg>(sm, ms, tmem, a, cur.b, head_base, heads_here, warp, lane);
       fence_proxy_async_smem();
       fence_before_sync();
       __syncwarp();
@@ -898,6 +917,11 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
   }
 }
 
+// Two instances: kQImg, Q operand images from the prep kernel in the workspace
+// (the serving path), and without them, Q quantised here at each piece start;
+// the second's code stays out of the first (the kernel is bound by
+// instruction fetch).
+template <bool kQImg>
 __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __grid_constant__ DecodeArgs a,
                                                                   const __grid_constant__ CacheMaps maps) {
   // the merge kernel (launched next as a programmatic dependent) may be
@@ -1001,7 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
     loader(sm, ms, tmem, sc, warp, lane, a);
   } else {
     setmaxnreg_inc<kSoftmaxRegs>();
-    softmax(sm, ms, tmem, sc, head_base, heads_here, warp, lane, a.sm_scale * kLog2e, a);
+    softmax<kQImg>(sm, ms, tmem, sc, head_base, heads_here, warp, lane, a.sm_scale * kLog2e, a);
   }
 
   fence_before_sync();
@@ -1043,12 +1067,14 @@ cudaError_t launch_q_prep_fp4(const DecodeArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(mla_decode_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  cudaError_t e = cudaFuncSetAttribute(mla_decode_fp4_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(mla_decode_fp4_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
   const int head_blocks = (a.num_heads + kNH - 1) / kNH;
   const dim3 grid = a.balanced ? dim3(a.num_splits * head_blocks, 1, 1) : dim3(a.num_splits * head_blocks, a.batch, 1);
   if (!a.q_img) {
-    mla_decode_fp4_kernel<<<grid, kThreads, kSmem, stream>>>(a, maps);
+    mla_decode_fp4_kernel<false><<<grid, kThreads, kSmem, stream>>>(a, maps);
     return cudaGetLastError();
   }
   // after the Q prep kernel: start while it runs (everything before the Q
@@ -1063,7 +1089,7 @@ cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mla_decode_fp4_kernel, a, maps);
+  return cudaLaunchKernelEx(&cfg, mla_decode_fp4_kernel<true>, a, maps);
 }
 
 }  // namespace kimi

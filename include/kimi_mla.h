@@ -155,17 +155,20 @@ typedef struct KimiMlaDecodeParams {
  * num_kv_splits = S > 0 cuts every sequence into S equal ranges of 128-token
  * tiles, as the reference's num_kv_splits does (S = 1 needs no workspace).
  * num_kv_splits = 0 selects the balanced schedule: the batch's tiles are laid
- * end to end and split evenly over one CTA per SM per 64-head block, so
+ * end to end and split evenly over one CTA per SM per head block, so
  * ragged batches and batches smaller than the SM count keep every SM busy;
  * sequences that one CTA covers are written directly, the others merged.
+ * A head block is 64 heads, or 16 when num_heads <= 16 (a tensor-parallel
+ * shard such as 8 heads per GPU).
  * The workspace holds slots x heads x 1028 bytes of partials (bf16 rows and
  * fp32 log-sum-exps; slots = batch x S, or batch + CTAs when balanced), 8
- * bytes per sequence when balanced, and 60416 bytes of Q operands per
- * sequence and 64-head block, each part rounded up to 256 bytes. */
+ * bytes per sequence when balanced, and Q operands per sequence and head
+ * block (60416 bytes for a 64-head block, 15104 for a 16-head block), each
+ * part rounded up to 256 bytes. */
 KIMI_API size_t kimi_mla_decode_workspace_size(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
 
 /* S for num_kv_splits = S > 0 (capped at 64); for 0, the balanced schedule's
- * CTAs per 64-head block on the current device. */
+ * CTAs per head block on the current device. */
 KIMI_API int32_t kimi_mla_decode_num_splits(int32_t batch, int32_t num_heads, int32_t num_kv_splits);
 
 /* Absorbed-MLA decode, one query token per sequence, one KV head. */

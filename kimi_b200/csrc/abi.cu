@@ -128,7 +128,8 @@ bool encode_bf16_map(CUtensorMap& m, const void* base, cuuint32_t rank, const cu
 // How one call is laid out on the GPU.
 //  * requested splits S > 0: split mode, every sequence cut into S equal tile
 //    ranges (the reference's num_kv_splits), S = 1 writing the output directly;
-//  * requested 0 (auto): balanced mode, one CTA per SM and 64-head block,
+//  * requested 0 (auto): balanced mode, one CTA per SM and head block (64
+//    heads, or 16 for calls with at most 16 heads),
 //    each a run over the batch's tiles laid end to end (see DecodeArgs in
 //    kernels.cuh).
 struct Plan {
@@ -137,7 +138,8 @@ struct Plan {
 };
 
 Plan resolve_plan(int32_t /*batch*/, int32_t num_heads, int32_t requested) {
-  const int head_blocks = (num_heads + 63) / 64;
+  const int nh = kimi::decode_heads_per_cta(num_heads);
+  const int head_blocks = (num_heads + nh - 1) / nh;
   if (requested > 0) return {false, requested > KIMI_MLA_MAX_SPLITS ? KIMI_MLA_MAX_SPLITS : requested};
   const int c = device_sm_count() / head_blocks;  // one CTA per SM and head block
   return {true, c < 1 ? 1 : c};
@@ -148,7 +150,8 @@ inline size_t round256(size_t n) { return (n + 255) & ~static_cast<size_t>(255);
 // Workspace: partial outputs [slots, heads, 512] bf16 (each normalised by its own
 // softmax sum, so bf16 costs one rounding like the output's), log-sum-exps [slots,
 // heads] fp32, then (balanced mode) [batch] int2 CTA spans, then the Q
-// operand images [batch][head blocks] of kQImageBytes.  Split mode has
+// operand images [batch][head blocks] of q_image_bytes(nh) (nh heads per block:
+// 64, or 16 for calls with at most 16 heads).  Split mode has
 // batch * S slots (none for S = 1, and no workspace at all: the decode kernel
 // then quantises Q itself, one piece per CTA), balanced mode batch + ctas.
 struct Layout {
@@ -163,7 +166,8 @@ Layout workspace_layout(int64_t batch, int64_t heads, const Plan& plan) {
   l.po_bytes = round256(l.slots * heads * kLatent * sizeof(__nv_bfloat16));
   l.lse_bytes = round256(l.slots * heads * sizeof(float));
   l.meta_bytes = plan.balanced ? round256(static_cast<size_t>(batch) * 2 * sizeof(int32_t)) : 0;
-  l.qimg_bytes = round256(static_cast<size_t>(batch) * ((heads + 63) / 64) * kimi::kQImageBytes);
+  const int nh = kimi::decode_heads_per_cta(static_cast<int>(heads));
+  l.qimg_bytes = round256(static_cast<size_t>(batch) * ((heads + nh - 1) / nh) * kimi::q_image_bytes(nh));
   return l;
 }
 

@@ -315,12 +315,16 @@ __device__ void balanced_schedule(const DecodeArgs& a, SchedScratch& ms, Sched& 
   __syncthreads();  // the scan scratch is reused
 }
 
-// Transpose-reduce (max or sum) of 32 per-lane values over the warp: lane j
-// ends with the reduction of element j across all 32 lanes.
-template <bool kMax>
-__device__ __forceinline__ float warp_transpose_reduce(float (&v)[32], int lane) {
+// Transpose-reduce (max or sum) of N per-lane values over the warp (N a
+// power of two, at most 32): lane l ends with the reduction of element l % N
+// across all 32 lanes.  The exchange steps halve the values held per lane
+// (each keeps one half and combines it with the partner's same half); with
+// N < 32 a butterfly over the remaining lane bits finishes the reduction.
+template <bool kMax, int N = 32>
+__device__ __forceinline__ float warp_transpose_reduce(float (&v)[N], int lane) {
+  static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N is a power of two up to 32");
 #pragma unroll
-  for (int width = 16; width >= 1; width >>= 1) {
+  for (int width = N / 2; width >= 1; width >>= 1) {
     const bool upper = (lane & width) != 0;
 #pragma unroll
     for (int j = 0; j < width; ++j) {
@@ -330,7 +334,13 @@ __device__ __forceinline__ float warp_transpose_reduce(float (&v)[32], int lane)
       v[j] = kMax ? fmaxf(keep, got) : keep + got;
     }
   }
-  return v[0];
+  float r = v[0];
+#pragma unroll
+  for (int width = N; width < 32; width <<= 1) {
+    const float got = __shfl_xor_sync(0xffffffffu, r, width);
+    r = kMax ? fmaxf(r, got) : r + got;
+  }
+  return r;
 }
 
 }  // namespace dec

@@ -18,14 +18,22 @@ constexpr int kTokenBytes = 384;  // nibbles + RoPE per token in kv_buffer
 constexpr int kScaleBytes = 16;
 constexpr int kPageBytes = kPageSize * kTokenBytes;        // 24576
 constexpr int kPageScaleBytes = kPageSize * kScaleBytes;   // 1024
-// Q operands of the fp4 kernel for one (sequence, 64-head block), as the
-// shared-memory images its QK^T MMAs read: three block-scaled e2m1 terms
-// (2 K blocks x 192 rows x 128 B, 128-byte swizzle), q_pe (64 rows x 128 B,
-// same swizzle), then the terms' e8m0 scales as [192 rows][16 blocks].
-constexpr int kQTermBytes = 2 * 192 * 128;   // 49152
-constexpr int kQPeBytes = 64 * 128;          // 8192
-constexpr int kQScaleBytes = 192 * 16;       // 3072
-constexpr int kQImageBytes = kQTermBytes + kQPeBytes + kQScaleBytes;  // 60416
+// Heads per CTA of the fp4 decode: 64, or 16 for a call with at most 16
+// heads (a tensor-parallel shard: 8 heads of Kimi-K2 or 16 of DeepSeek-V3 at
+// TP8), whose MMAs and softmax then work on 16 head columns instead of 64.
+__host__ __device__ constexpr int decode_heads_per_cta(int num_heads) { return num_heads <= 16 ? 16 : 64; }
+
+// Q operands of the fp4 kernel for one (sequence, head block of nh heads), as
+// the shared-memory images its QK^T MMAs read: three block-scaled e2m1 terms
+// (2 K blocks x 3 nh rows x 128 B, 128-byte swizzle), q_pe (nh rows x 128 B,
+// same swizzle), then the terms' e8m0 scales as [3 nh rows][16 blocks].
+__host__ __device__ constexpr int q_term_bytes(int nh) { return 2 * 3 * nh * 128; }
+__host__ __device__ constexpr int q_pe_bytes(int nh) { return nh * 128; }
+__host__ __device__ constexpr int q_scale_bytes(int nh) { return 3 * nh * 16; }
+__host__ __device__ constexpr int q_image_bytes(int nh) { return q_term_bytes(nh) + q_pe_bytes(nh) + q_scale_bytes(nh); }
+constexpr int kQImageBytes = q_image_bytes(64);       // 60416 (64-head blocks)
+constexpr int kQImageBytesSmall = q_image_bytes(16);  // 15104 (16-head blocks)
+static_assert(kQImageBytes == 60416 && kQImageBytesSmall == 15104, "Q image sizes");
 
 // Bits of the decode's device status word (DecodeArgs::status): which wait
 // gave up, or a page id outside the cache.

@@ -64,7 +64,7 @@ namespace {
 using namespace sm100;
 using namespace dec;
 
-constexpr int kNH = 64;  // heads per CTA
+constexpr int kNHMax = 64;  // heads per CTA of the wide form (the small form has 16)
 constexpr int kSoftmaxWarps = 8;
 constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr int kLoaderWarp0 = 8;  // warps 8..15
@@ -103,16 +103,34 @@ constexpr int kOffSc = kOffNib + 2 * kNibStage;
 constexpr int kOffKpe = kOffSc + kScSlots * kScStage;  // k_pe: 128 rows x 128 bytes
 constexpr int kVCol = 16384;                // V'': one 128-latent column (16 atoms of 8 tokens)
 constexpr int kOffV = kOffKpe + 128 * 128;  // one tile, four latent columns; ring of 4 token quarters
-constexpr int kQBlock = 192 * 128;          // Q terms: 192 rows x 128 bytes per K column block
-constexpr int kOffQ = kOffV + 4 * kVCol;
-constexpr int kOffQpe = kOffQ + 2 * kQBlock;  // q_pe bf16: 64 rows x 128 bytes
-constexpr int kOffP = kOffQpe + 64 * 128;     // P'' hi e4m3, MN-major cores (token group 0..15, head bytes 0..3)
-constexpr int kOffPlo = kOffP + 8192;         // P'' lo (residual), same layout
-constexpr int kPRow = 4 * 128;
-constexpr int kOffMisc = kOffPlo + 8192;
-static_assert(kOffKpe % 1024 == 0 && kOffV % 1024 == 0 && kOffQ % 1024 == 0 && kOffQpe % 1024 == 0 &&
-                  kOffP % 1024 == 0,
-              "swizzled operands start on 1 KB boundaries");
+constexpr int kOffQ = kOffV + 4 * kVCol;    // Q terms, then q_pe, P'' and (small form) the epilogue stage
+static_assert(kOffKpe % 1024 == 0 && kOffV % 1024 == 0 && kOffQ % 1024 == 0, "swizzled operands start on 1 KB boundaries");
+
+// The part of the layout that depends on the heads per CTA, NH = 64 (wide
+// form) or 16 (small form, calls with at most 16 heads).
+template <int NH>
+struct Form {
+  static constexpr int kQRows = 3 * NH;               // B rows of the latent QK MMA: three Q terms
+  static constexpr int kQBlock = kQRows * 128;        // Q terms: kQRows rows x 128 bytes per K column block
+  static constexpr int kOffQpe = kOffQ + 2 * kQBlock;  // q_pe bf16: NH rows x 128 bytes
+  // P'' hi e4m3, MN-major cores: per 8-token group NH / 16 core matrices of
+  // 8 tokens x 16 head bytes; then P'' lo (residual) in the same layout
+  static constexpr int kPRow = NH / 16 * 128;
+  static constexpr int kPBytes = 16 * kPRow;          // 128 tokens
+  static constexpr int kOffP = kOffQpe + NH * 128;
+  static constexpr int kOffPlo = kOffP + kPBytes;
+  // epilogue transposes: 2 KB per softmax warp, in P'' (wide form; its last
+  // PV is complete) or in a stage of their own (small form)
+  static constexpr int kOffStage = NH == 64 ? kOffP : kOffPlo + kPBytes;
+  static constexpr int kOffMisc = NH == 64 ? kOffPlo + kPBytes : kOffStage + kSoftmaxWarps * 2048;
+  // TMEM: S as three term column groups of NH, O as four 128-latent chunks of
+  // NH head columns (wide: hi and lo accumulate together) or 2 NH (small: hi
+  // then lo columns, one N = 32 MMA per chunk and K step)
+  static constexpr uint32_t kOChunkCols = NH == 64 ? 64 : 2 * NH;
+  static_assert(kOffQpe % 1024 == 0 && kOffP % 1024 == 0, "swizzled operands start on 1 KB boundaries");
+  static_assert(kOffP + kQRows * kScaleBytes <= kOffMisc, "Q scale staging fits in P''");
+  static_assert(2 * kQBlock == q_term_bytes(NH) && NH * 128 == q_pe_bytes(NH), "Q image layout");
+};
 
 struct Misc {
   uint64_t mb_rawfull[2];    // nibble stage s landed (producer expect_tx + TMA bytes)
@@ -137,31 +155,34 @@ struct Misc {
   int abort_flag;
   int tile_smax[4];          // max e8m0 byte of tile j in slot j % 4 (reset two tiles ahead)
   int sig[4];                // reference exponent sigma of tile j in slot j % 4
-  alignas(16) float R[kNH];  // per-head exp2 offset, log2 units (read as float4)
-  float alpha[kNH];          // O rescale factors of the current event
-  float beta[kNH];           // softmax-sum rescale factors of the current event
-  float red[4][kNH];         // cross-warp reduction scratch
+  alignas(16) float R[kNHMax];  // per-head exp2 offset, log2 units (read as float4)
+  float alpha[kNHMax];          // O rescale factors of the current event
+  float beta[kNHMax];           // softmax-sum rescale factors of the current event
+  float red[4][kNHMax];         // cross-warp reduction scratch
 };
-constexpr int kSmem = kOffMisc + static_cast<int>(sizeof(Misc));
-static_assert(kSmem <= 232448, "shared memory budget");
-static_assert(kOffMisc % 16 == 0 && offsetof(Misc, R) % 16 == 0, "per-head arrays are read with 16-byte loads");
-static_assert(kOffP + 192 * kScaleBytes <= kOffMisc, "Q scale staging fits in P''");
-static_assert(kQTermBytes == 2 * kQBlock && kOffQpe == kOffQ + kQTermBytes && kQPeBytes == 64 * 128,
-              "the Q image's terms and q_pe land with one bulk copy");
+template <int NH>
+constexpr int smem_bytes() { return Form<NH>::kOffMisc + static_cast<int>(sizeof(Misc)); }
+static_assert(smem_bytes<64>() <= 232448 && smem_bytes<16>() <= 232448, "shared memory budget");
+static_assert(Form<64>::kOffMisc % 16 == 0 && Form<16>::kOffMisc % 16 == 0 && offsetof(Misc, R) % 16 == 0,
+              "per-head arrays are read with 16-byte loads");
 
 __device__ __forceinline__ uint8_t* smem_base() {
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
   return dyn_smem;
 }
 
-// The grid's x index interleaves the 64-head blocks fastest: CTA x is head
+// The grid's x index interleaves the head blocks fastest: CTA x is head
 // block x % head_blocks of schedule CTA (split) x / head_blocks, so the CTAs
 // that read the same tiles for different head blocks run side by side and
 // the second read is an L2 hit.
-__device__ __forceinline__ int head_blocks(const DecodeArgs& a) { return (a.num_heads + kNH - 1) / kNH; }
-__device__ __forceinline__ int cta_index(const DecodeArgs& a) { return static_cast<int>(blockIdx.x) / head_blocks(a); }
-__device__ __forceinline__ int cta_count(const DecodeArgs& a) { return static_cast<int>(gridDim.x) / head_blocks(a); }
-__device__ __forceinline__ int head_block(const DecodeArgs& a) { return static_cast<int>(blockIdx.x) % head_blocks(a); }
+template <int NH>
+__device__ __forceinline__ int head_blocks(const DecodeArgs& a) { return (a.num_heads + NH - 1) / NH; }
+template <int NH>
+__device__ __forceinline__ int cta_index(const DecodeArgs& a) { return static_cast<int>(blockIdx.x) / head_blocks<NH>(a); }
+template <int NH>
+__device__ __forceinline__ int cta_count(const DecodeArgs& a) { return static_cast<int>(gridDim.x) / head_blocks<NH>(a); }
+template <int NH>
+__device__ __forceinline__ int head_block(const DecodeArgs& a) { return static_cast<int>(blockIdx.x) % head_blocks<NH>(a); }
 
 __device__ __forceinline__ void record_status(const DecodeArgs& a, int bits) {
   if (a.status) atomicOr(a.status, bits);
@@ -315,9 +336,11 @@ __device__ void producer(uint8_t* sm, Misc& ms, const Sched& sc, const DecodeArg
 // ---------------------------------------------------------------------------
 // Issuers (warp 16: QK, warps 17-18: PV; lane 0 issues)
 // ---------------------------------------------------------------------------
+template <int NH>
 __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int lane, const DecodeArgs& a) {
-  const uint32_t id_pe = instr_desc(kFmtBF16, kFmtBF16, false, false, 128, 64);
-  const uint32_t sQ = smem_addr(sm + kOffQ), sQpe = smem_addr(sm + kOffQpe), sKpe = smem_addr(sm + kOffKpe);
+  using F = Form<NH>;
+  const uint32_t id_pe = instr_desc(kFmtBF16, kFmtBF16, false, false, 128, NH);
+  const uint32_t sQ = smem_addr(sm + kOffQ), sQpe = smem_addr(sm + F::kOffQpe), sKpe = smem_addr(sm + kOffKpe);
   Cursor cur;
   cursor_start(a, sc, cur);
   int pieces = 0;
@@ -351,7 +374,31 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
       if (first) ++pieces;
     }
     fence_after_sync();
-    if (lane == 0) {
+    if (lane == 0 && NH == 16) {
+      // small form: latent first (8 K steps of 64, N = 48: the three terms of
+      // 16 heads, the first step starting S), then the RoPE MMAs add
+      // k_pe . q_pe^T onto the term-0 columns
+      const uint32_t sA = smem_addr(sm + kOffNib + s * kNibStage);
+      const uint32_t sfa0 = tmem + kColSfa + 16 * s, sfb0 = tmem + kColSfb;
+#pragma unroll 1
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t koff = (k & 3) * 32;
+        const uint32_t byte = 2 * (k & 1);
+        const uint32_t sfa = (sfa0 + 4 * (k >> 1)) | (byte << 30);
+        const uint32_t sfb = (sfb0 + 8 * (k >> 1)) | (byte << 30);
+        const uint64_t da = smem_desc(sA + (k >> 2) * kNibBlock + koff, 16, 1024, kSwizzle128B);
+        const uint32_t qb = sQ + (k >> 2) * F::kQBlock + koff;
+        mma_mxf4_ss(tmem + kColS, da, smem_desc(qb, 16, 1024, kSwizzle128B), instr_desc_mxf4(F::kQRows, byte, byte),
+                    sfa, sfb, k > 0 ? 1u : 0u);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma_f16_ss(tmem + kColS, smem_desc(sKpe + 32 * k, 16, 1024, kSwizzle128B),
+                   smem_desc(sQpe + 32 * k, 16, 1024, kSwizzle128B), id_pe, 1u);
+      mma_commit(&ms.mb_kpefree);
+      mma_commit(&ms.mb_sfull);
+      mma_commit(&ms.mb_qkdone[s]);
+    } else if (lane == 0) {
       // RoPE first (k_pe is single-buffered): S[:, 0:64) = k_pe . q_pe^T
 #pragma unroll
       for (int k = 0; k < 4; ++k)
@@ -369,7 +416,7 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
         const uint32_t sfa = (sfa0 + 4 * (k >> 1)) | (byte << 30);
         const uint32_t sfb = (sfb0 + 8 * (k >> 1)) | (byte << 30);
         const uint64_t da = smem_desc(sA + (k >> 2) * kNibBlock + koff, 16, 1024, kSwizzle128B);
-        const uint32_t qb = sQ + (k >> 2) * kQBlock + koff;
+        const uint32_t qb = sQ + (k >> 2) * F::kQBlock + koff;
         if (k == 0) {
           mma_mxf4_ss(tmem + kColS, da, smem_desc(qb, 16, 1024, kSwizzle128B), instr_desc_mxf4(64, byte, byte),
                       sfa, sfb, 1u);
@@ -389,10 +436,15 @@ __device__ void qk_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
 
 // PV issuer h owns latent half h (chunks 2h, 2h + 1) and walks the tile's
 // four token quarters as the loaders finish them.
+// Small form: P'' hi and lo are one N = 32 B operand (the lo cores one
+// P'' buffer further on), so each chunk and K step is one MMA into 32 columns
+// of O (hi heads, then lo heads) instead of two into the same 64.
+template <int NH>
 __device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int lane, int h,
                           const DecodeArgs& a) {
-  const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, 64);
-  const uint32_t sP = smem_addr(sm + kOffP), sPlo = smem_addr(sm + kOffPlo);
+  using F = Form<NH>;
+  const uint32_t id_pv = instr_desc(kFmtE5M2, kFmtE4M3, true, true, 128, NH == 64 ? 64 : 2 * NH);
+  const uint32_t sP = smem_addr(sm + F::kOffP), sPlo = smem_addr(sm + F::kOffPlo);
   const uint32_t sV = smem_addr(sm + kOffV + 2 * h * kVCol);
   Cursor cur;
   cursor_start(a, sc, cur);
@@ -405,9 +457,17 @@ __device__ void pv_issuer(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc,
       ok = warp_wait(&ms.mb_pfull[k], par, ms, a, 32, lane) && warp_wait(&ms.mb_vfull[k], par, ms, a, 32, lane);
       if (!ok) break;
       fence_after_sync();
-      if (lane == 0) {
-        const uint64_t phi = smem_desc(sP + k * 4 * kPRow, kPRow, 128);
-        const uint64_t plo = smem_desc(sPlo + k * 4 * kPRow, kPRow, 128);
+      if (lane == 0 && NH == 16) {
+        const uint64_t pb = smem_desc(sP + k * 4 * F::kPRow, F::kPRow, F::kPBytes);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          mma_f8f6f4_ss(tmem + kColO + F::kOChunkCols * (2 * h + c),
+                        smem_desc(sV + c * kVCol + k * 4096, kVCol, 1024, kSwizzle128B), pb, id_pv,
+                        (fresh && k == 0) ? 0u : 1u);
+        mma_commit(&ms.mb_pvq[k]);
+      } else if (lane == 0) {
+        const uint64_t phi = smem_desc(sP + k * 4 * F::kPRow, F::kPRow, 128);
+        const uint64_t plo = smem_desc(sPlo + k * 4 * F::kPRow, F::kPRow, 128);
 #pragma unroll
         for (int c = 0; c < 2; ++c)
           mma_f8f6f4_ss(tmem + kColO + 64 * (2 * h + c),
@@ -551,13 +611,16 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, in
 }
 
 // ---------------------------------------------------------------------------
-// Q of one sequence (256 threads: 4 per head; part p handles the 32-element
-// blocks 4p .. 4p + 3 of the latent and 16-byte chunks 2p, 2p + 1 of q_pe).
-// Writes the QK operand images: the terms at qdst (the layout of kOffQ), q_pe
-// at pedst (the layout of kOffQpe) and the terms' scale bytes at sfdst as
-// [192 rows][16 blocks].  Used in shared memory by the decode kernel (no
+// Q of one sequence for a block of NH heads (256 threads: 256 / NH per head;
+// with 4 per head (NH = 64) part p handles the 32-element blocks 4p .. 4p + 3
+// of the latent and 16-byte chunks 2p, 2p + 1 of q_pe, with 16 per head
+// (NH = 16) block p and chunk p < 8).  Writes the QK operand images: the terms
+// at qdst (the layout of kOffQ: term t of head h is row NH t + h), q_pe at
+// pedst (the layout of the form's kOffQpe) and the terms' scale bytes at sfdst
+// as [3 NH rows][16 blocks].  Used in shared memory by the decode kernel (no
 // workspace) and in global memory by the Q prep kernel.
 // ---------------------------------------------------------------------------
+template <int NH>
 __device__ __forceinline__ void q_block(const uint4 (&v)[4], int h, int bl, uint8_t* qdst, uint8_t* sfdst) {
   float x[32];
 #pragma unroll
@@ -591,44 +654,52 @@ __device__ __forceinline__ void q_block(const uint4 (&v)[4], int h, int bl, uint
         x[2 * i + 1] -= __half2float(__ushort_as_half(static_cast<unsigned short>(h2 >> 16))) * scl;
       }
     }
-    const int n = 64 * t + h;
-    *reinterpret_cast<uint4*>(qdst + (bl >> 3) * kQBlock + (n >> 3) * 1024 + sw128_offset(n & 7, bl & 7)) =
+    const int n = NH * t + h;
+    *reinterpret_cast<uint4*>(qdst + (bl >> 3) * Form<NH>::kQBlock + (n >> 3) * 1024 + sw128_offset(n & 7, bl & 7)) =
         make_uint4(w[0], w[1], w[2], w[3]);
     sfdst[n * kScaleBytes + bl] = static_cast<uint8_t>(e + 127);
   }
 }
 
+template <int NH>
 __device__ void q_operands(const DecodeArgs& a, int b, int head_base, int heads_here, int tid, uint8_t* qdst,
                            uint8_t* pedst, uint8_t* sfdst) {
-  const int h = tid >> 2, part = tid & 3;
+  constexpr int kParts = kSoftmaxThreads / NH;    // threads per head
+  constexpr int kBlocks = 16 / kParts;            // 32-element blocks per thread
+  constexpr int kPeChunks = kParts >= 8 ? 1 : 8 / kParts;  // 16-byte q_pe chunks per thread
+  const int h = tid / kParts, part = tid % kParts;
   const bool live = h < heads_here;
   const __nv_bfloat16* qrow = a.q + b * a.q_stride_b + (head_base + h) * a.q_stride_h;
 #pragma unroll 1
-  for (int blk = 0; blk < 4; ++blk) {
+  for (int blk = 0; blk < kBlocks; ++blk) {
     uint4 v[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) v[k] = ldg_stream_if(qrow + 32 * (4 * part + blk) + 8 * k, live);
-    q_block(v, h, 4 * part + blk, qdst, sfdst);
+    for (int k = 0; k < 4; ++k) v[k] = ldg_stream_if(qrow + 32 * (kBlocks * part + blk) + 8 * k, live);
+    q_block<NH>(v, h, kBlocks * part + blk, qdst, sfdst);
   }
+  if (kPeChunks * part < 8) {
 #pragma unroll
-  for (int k = 0; k < 2; ++k)
-    *reinterpret_cast<uint4*>(pedst + (h >> 3) * 1024 + sw128_offset(h & 7, 2 * part + k)) =
-        ldg_stream_if(qrow + kLatent + 8 * (2 * part + k), live);
+    for (int k = 0; k < kPeChunks; ++k)
+      *reinterpret_cast<uint4*>(pedst + (h >> 3) * 1024 + sw128_offset(h & 7, kPeChunks * part + k)) =
+          ldg_stream_if(qrow + kLatent + 8 * (kPeChunks * part + k), live);
+  }
 }
 
 // B scale factors of the Q terms into TMEM (softmax warps 0-3, one TMEM lane
 // quarter each): column 8 k4 + n1 of lane n0 (every quarter alike) holds the
-// scale word k4 of row n0 + 32 n1 (rows >= 192 are not read).  `global` says
-// whether sf ([192][16] bytes) lies in global memory.
+// scale word k4 of row n0 + 32 n1 (rows >= 3 NH are not read).  `global` says
+// whether sf ([3 NH][16] bytes) lies in global memory.
+template <int NH>
 __device__ __forceinline__ void store_q_scales(uint32_t tmem, const uint8_t* sf, bool global, int warp, int lane) {
+  constexpr int kRows = Form<NH>::kQRows;
   uint32_t u[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const int n = lane + 32 * (i & 7);
-    const uint8_t* src = sf + min(n, 191) * kScaleBytes + 4 * (i >> 3);
+    const uint8_t* src = sf + min(n, kRows - 1) * kScaleBytes + 4 * (i >> 3);
     const uint32_t w = global ? static_cast<uint32_t>(ldg_s32_or(reinterpret_cast<const int32_t*>(src), true, 0))
                               : *reinterpret_cast<const uint32_t*>(src);
-    u[i] = n < 192 ? w : 0x7F7F7F7Fu;
+    u[i] = n < kRows ? w : 0x7F7F7F7Fu;
   }
   tmem_st32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + kColSfb, u);
   tmem_st_wait();
@@ -637,43 +708,57 @@ __device__ __forceinline__ void store_q_scales(uint32_t tmem, const uint8_t* sf,
 // Q operands of a new piece's sequence (softmax threads).  With Q images in
 // the workspace: one bulk copy of the terms and q_pe (completing mb_qload)
 // and the scale factors from global memory; otherwise quantised here.
-template <bool kQImg>
+template <int NH, bool kQImg>
 __device__ void build_q(uint8_t* sm, Misc& ms, uint32_t tmem, const DecodeArgs& a, int b, int head_base,
                         int heads_here, int warp, int lane) {
+  using F = Form<NH>;
+  constexpr uint32_t kLoadBytes = q_term_bytes(NH) + q_pe_bytes(NH);
   const int tid = threadIdx.x;
   if constexpr (kQImg) {
-    const uint8_t* img = a.q_img + (static_cast<int64_t>(b) * head_blocks(a) + head_block(a)) * kQImageBytes;
+    const uint8_t* img =
+        a.q_img + (static_cast<int64_t>(b) * head_blocks<NH>(a) + head_block<NH>(a)) * q_image_bytes(NH);
     asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the Q prep grid is complete (no-op later)
     if (tid == 0) {
-      mbar_arrive_expect_tx(&ms.mb_qload, kQTermBytes + kQPeBytes);
-      bulk_load(sm + kOffQ, img, kQTermBytes + kQPeBytes, &ms.mb_qload);
+      mbar_arrive_expect_tx(&ms.mb_qload, kLoadBytes);
+      bulk_load(sm + kOffQ, img, kLoadBytes, &ms.mb_qload);
     }
-    if (tid < kNH) ms.R[tid] = 0.f;
-    if (warp < 4) store_q_scales(tmem, img + kQTermBytes + kQPeBytes, true, warp, lane);
+    if (tid < NH) ms.R[tid] = 0.f;
+    if (warp < 4) store_q_scales<NH>(tmem, img + kLoadBytes, true, warp, lane);
   } else {
-    uint8_t* sf_stage = sm + kOffP;  // [192 rows][16] e8m0 (P'' is free at a piece start)
-    q_operands(a, b, head_base, heads_here, tid, sm + kOffQ, sm + kOffQpe, sf_stage);
-    if ((tid & 3) == 0) ms.R[tid >> 2] = 0.f;
+    uint8_t* sf_stage = sm + F::kOffP;  // [3 NH rows][16] e8m0 (P'' is free at a piece start)
+    q_operands<NH>(a, b, head_base, heads_here, tid, sm + kOffQ, sm + F::kOffQpe, sf_stage);
+    if (tid < NH) ms.R[tid] = 0.f;
     named_bar(kBarSoftmax, kSoftmaxThreads);  // the scale bytes are staged
-    if (warp < 4) store_q_scales(tmem, sf_stage, false, warp, lane);
+    if (warp < 4) store_q_scales<NH>(tmem, sf_stage, false, warp, lane);
   }
 }
 
 // ---------------------------------------------------------------------------
 // Softmax warps (0..7) and the per-piece epilogue
 // ---------------------------------------------------------------------------
-template <bool kQImg>
+// HT = NH / 2 heads per thread: warp w takes TMEM lane quadrant (token
+// quarter) w % 4 and heads HT (w / 4) .. HT (w / 4) + HT - 1.
+template <int HT>
+__device__ __forceinline__ void tmem_ld_heads(uint32_t taddr, uint32_t (&r)[HT]) {
+  if constexpr (HT == 32) tmem_ld32(taddr, r);
+  else tmem_ld8(taddr, r);
+}
+
+template <int NH, bool kQImg>
 __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, int head_base, int heads_here,
                         int warp, int lane, float c_log2, const DecodeArgs& a) {
+  using F = Form<NH>;
+  constexpr int HT = NH / 2;
+  static_assert(HT == 32 || HT == 8, "heads per softmax thread");
   const int tid = threadIdx.x;
   const int q = warp & 3;                  // TMEM lane quadrant
-  const int hf = warp >> 2;                // heads 32 hf .. 32 hf + 31
+  const int hf = warp >> 2;                // heads HT hf .. HT hf + HT - 1
   const int st = 32 * q + lane;            // softmax token
   const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
 
-  float l_part[32];
+  float l_part[HT];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
+  for (int j = 0; j < HT; ++j) l_part[j] = 0.f;
   int sigma_prev = 0;
   Cursor cur;
   cursor_start(a, sc, cur);
@@ -684,7 +769,7 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     if (first) {
       // a new sequence: its Q replaces the previous one (whose last QK is
       // complete: its S was read; its last PV too: the epilogue waited for it)
-      build_q<kQImg>(sm, ms, tmem, a, cur.b, head_base, heads_here, warp, lane);
+      build_q<NH, kQImg>(sm, ms, tmem, a, cur.b, head_base, heads_here, warp, lane);
       fence_proxy_async_smem();
       fence_before_sync();
       __syncwarp();
@@ -693,23 +778,23 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     }
     bool ok = warp_wait(&ms.mb_sfull, par, ms, a, 1, lane);
     fence_after_sync();
-    float t[32];
+    float t[HT];
     int sigma_cur = sigma_prev;
     if (ok) {
       {
-        uint32_t sv[32];
-        tmem_ld32(tmem + lane_base + kColS + 32 * hf, sv);
+        uint32_t sv[HT];
+        tmem_ld_heads<HT>(tmem + lane_base + kColS + HT * hf, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(sv[j]);
-        tmem_ld32(tmem + lane_base + kColS + 64 + 32 * hf, sv);
+        for (int j = 0; j < HT; ++j) t[j] = __uint_as_float(sv[j]);
+        tmem_ld_heads<HT>(tmem + lane_base + kColS + NH + HT * hf, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] += __uint_as_float(sv[j]);
-        tmem_ld32(tmem + lane_base + kColS + 128 + 32 * hf, sv);
+        for (int j = 0; j < HT; ++j) t[j] += __uint_as_float(sv[j]);
+        tmem_ld_heads<HT>(tmem + lane_base + kColS + 2 * NH + HT * hf, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] += __uint_as_float(sv[j]);
+        for (int j = 0; j < HT; ++j) t[j] += __uint_as_float(sv[j]);
       }
       fence_before_sync();
       __syncwarp();
@@ -718,22 +803,22 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
       sigma_cur = ms.sig[tile & 3];
       const bool tvalid = st < cursor_valid(cur);
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[32 * hf + j]);
+      for (int j = 0; j < HT; j += 4) {
+        const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[HT * hf + j]);
         const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) t[j + u] = tvalid ? fmaf(t[j + u], c_log2, -rv[u]) : -CUDART_INF_F;
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) t[j] = -CUDART_INF_F;
+      for (int j = 0; j < HT; ++j) t[j] = -CUDART_INF_F;
     }
     // rescale event: a piece's first tile, a score above R + 8.5, or a new sigma.
     // One barrier ORs "event or failure"; only when it is raised does a second
     // one tell a failure (leave the loop) from an event.
     float tmaxv = -CUDART_INF_F;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) tmaxv = fmaxf(tmaxv, t[j]);
+    for (int j = 0; j < HT; ++j) tmaxv = fmaxf(tmaxv, t[j]);
     const bool need =
         bar_or(kBarSoftmax, kSoftmaxThreads, !ok || first || tmaxv > 8.5f || sigma_cur != sigma_prev);
     if (need && bar_or(kBarSoftmax, kSoftmaxThreads, !ok)) break;
@@ -765,12 +850,13 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
       }
     };
     if (need) {
-      float v[32];
+      float v[HT];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = t[j];
-      ms.red[q][32 * hf + lane] = warp_transpose_reduce<true>(v, lane);  // tile max of x - R_old
+      for (int j = 0; j < HT; ++j) v[j] = t[j];
+      const float vmax = warp_transpose_reduce<true, HT>(v, lane);  // tile max of x - R_old, head lane % HT
+      if (lane < HT) ms.red[q][HT * hf + lane] = vmax;
       named_bar(kBarSoftmax, kSoftmaxThreads);
-      if (tid < kNH) {
+      if (tid < NH) {
         const float tm = fmaxf(fmaxf(ms.red[0][tid], ms.red[1][tid]), fmaxf(ms.red[2][tid], ms.red[3][tid]));
         // raise R so that this tile's max maps to 2^4 (only raise; a piece's first tile sets it)
         const float shift = first ? tm - 4.0f : fmaxf(tm - 4.0f, 0.0f);
@@ -782,22 +868,25 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
       }
       named_bar(kBarSoftmax, kSoftmaxThreads);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) t[j] -= ms.red[0][32 * hf + j];
+      for (int j = 0; j < HT; ++j) t[j] -= ms.red[0][HT * hf + j];
       if (!first) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) l_part[j] *= ms.beta[32 * hf + j];
+        for (int j = 0; j < HT; ++j) l_part[j] *= ms.beta[HT * hf + j];
         wait_pv_prev();
+        // O chunks 2 hf, 2 hf + 1 of this lane quadrant, 32 columns at a time:
+        // head column j (wide form), or hi / lo column of head j % 16 (small)
 #pragma unroll 1
         for (int cc = 0; cc < 2; ++cc) {
           const int c = 2 * hf + cc;
 #pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
+          for (int hh = 0; hh < static_cast<int>(F::kOChunkCols) / 32; ++hh) {
             uint32_t vv[32];
-            const uint32_t ta = tmem + lane_base + kColO + 64 * c + 32 * hh;
+            const uint32_t ta = tmem + lane_base + kColO + F::kOChunkCols * c + 32 * hh;
             tmem_ld32(ta, vv);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
+            for (int j = 0; j < 32; ++j)
+              vv[j] = __float_as_uint(__uint_as_float(vv[j]) * ms.alpha[NH == 64 ? 32 * hh + j : j % NH]);
             tmem_st32(ta, vv);
           }
         }
@@ -810,9 +899,9 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
 
     // ---- P'' = exp2(t) as e4m3 hi + residual, into the MN-major B operands ----
     {
-      uint32_t pw[8], pl[8];
+      uint32_t pw[HT / 4], pl[HT / 4];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
+      for (int j = 0; j < HT; j += 2) {
         const float p0 = ex2(t[j]);
         const float p1 = ex2(t[j + 1]);
         l_part[j] += p0;
@@ -828,11 +917,18 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
         }
       }
       wait_pvq_prev();
-      const int prow = (st >> 3) * kPRow + (st & 7) * 16;
-      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf) * 128) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-      *reinterpret_cast<uint4*>(sm + kOffP + prow + (2 * hf + 1) * 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
-      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf) * 128) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-      *reinterpret_cast<uint4*>(sm + kOffPlo + prow + (2 * hf + 1) * 128) = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+      const int prow = (st >> 3) * F::kPRow + (st & 7) * 16;
+      if constexpr (NH == 64) {
+        // heads 32 hf .. : two 16-head cores of each term
+        *reinterpret_cast<uint4*>(sm + F::kOffP + prow + (2 * hf) * 128) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+        *reinterpret_cast<uint4*>(sm + F::kOffP + prow + (2 * hf + 1) * 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+        *reinterpret_cast<uint4*>(sm + F::kOffPlo + prow + (2 * hf) * 128) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+        *reinterpret_cast<uint4*>(sm + F::kOffPlo + prow + (2 * hf + 1) * 128) = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+      } else {
+        // heads 8 hf .. 8 hf + 7: half of the one 16-head core row of each term
+        *reinterpret_cast<uint2*>(sm + F::kOffP + prow + 8 * hf) = make_uint2(pw[0], pw[1]);
+        *reinterpret_cast<uint2*>(sm + F::kOffPlo + prow + 8 * hf) = make_uint2(pl[0], pl[1]);
+      }
     }
     fence_proxy_async_smem();
     fence_before_sync();
@@ -845,18 +941,18 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     if (bar_or(kBarSoftmax, kSoftmaxThreads, !done)) break;
     fence_after_sync();
     {
-      const float s = warp_transpose_reduce<false>(l_part, lane);
-      ms.red[q][32 * hf + lane] = s;
+      const float s = warp_transpose_reduce<false, HT>(l_part, lane);
+      if (lane < HT) ms.red[q][HT * hf + lane] = s;
     }
 #pragma unroll
-    for (int j = 0; j < 32; ++j) l_part[j] = 0.f;
+    for (int j = 0; j < HT; ++j) l_part[j] = 0.f;
     // the piece covers its whole sequence -> final output; otherwise a partial in its slot
     const bool direct = a.balanced ? (cur.piece_begin == 0 && cur.piece_end == cursor_tiles(cur))
                                    : a.num_splits == 1;
-    const int64_t slot = a.balanced ? static_cast<int64_t>(cur.b) + cta_index(a)
-                                    : static_cast<int64_t>(cur.b) * a.num_splits + cta_index(a);
+    const int64_t slot = a.balanced ? static_cast<int64_t>(cur.b) + cta_index<NH>(a)
+                                    : static_cast<int64_t>(cur.b) * a.num_splits + cta_index<NH>(a);
     named_bar(kBarSoftmax, kSoftmaxThreads);
-    if (tid < kNH) {
+    if (tid < NH) {
       const float l = ms.red[0][tid] + ms.red[1][tid] + ms.red[2][tid] + ms.red[3][tid];
       // output factor 2^sigma / l per head (alpha is free again)
       ms.alpha[tid] = l > 0.f ? exp2f(static_cast<float>(sigma_prev)) / l : 0.f;
@@ -865,33 +961,37 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
     }
     if (a.balanced && tid == 0 && cur.piece_begin == 0) {
       // this CTA holds the sequence's first tile: record its CTA span for the merge
-      const int last_cta = cta_of_tile(cur.seq_pos + cursor_tiles(cur) - 1, sc, cta_count(a));
-      a.seq_meta[cur.b] = make_int2(cta_index(a), last_cta);
+      const int last_cta = cta_of_tile(cur.seq_pos + cursor_tiles(cur) - 1, sc, cta_count<NH>(a));
+      a.seq_meta[cur.b] = make_int2(cta_index<NH>(a), last_cta);
     }
     named_bar(kBarSoftmax, kSoftmaxThreads);
     // thread reads O^T lanes 32q.. of chunks 2hf, 2hf+1: latent d = 128c + 32q + lane.
-    // Each 32-latent x 32-head unit is transposed through this warp's 2 KB of
-    // the P'' area (idle: the piece's last PV is complete) into rows of
-    // 8 latents per head, stored as 16-byte vectors.
+    // Each 32-latent x 32-head unit (wide form; 32 x 16 in the small form,
+    // whose O holds each head's hi and lo sums apart) is transposed through
+    // this warp's 2 KB of the stage (the wide form's P'' area, idle: the
+    // piece's last PV is complete) into rows of 8 latents per head, stored as
+    // 16-byte vectors.
     const bool vec = !direct || ((reinterpret_cast<uintptr_t>(a.o) |
                                   static_cast<uintptr_t>(a.o_stride_b * 2) |
                                   static_cast<uintptr_t>(a.o_stride_h * 2)) & 15) == 0;
-    uint8_t* stage = sm + kOffP + warp * 2048;
+    uint8_t* stage = sm + F::kOffStage + warp * 2048;
+    constexpr int kUnitHeads = NH == 64 ? 32 : NH;  // heads of one transposed unit
 #pragma unroll 1
     for (int cc = 0; cc < 2; ++cc) {
       const int c = 2 * hf + cc;
 #pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
+      for (int hh = 0; hh < NH / kUnitHeads; ++hh) {
         uint32_t vv[32];
-        tmem_ld32(tmem + lane_base + kColO + 64 * c + 32 * hh, vv);
+        tmem_ld32(tmem + lane_base + kColO + F::kOChunkCols * c + 32 * hh, vv);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          reinterpret_cast<__nv_bfloat16*>(stage)[32 * j + lane] =
-              __float2bfloat16_rn(__uint_as_float(vv[j]) * ms.alpha[32 * hh + j]);
+        for (int j = 0; j < kUnitHeads; ++j) {
+          const float o = NH == 64 ? __uint_as_float(vv[j]) : __uint_as_float(vv[j]) + __uint_as_float(vv[j + NH]);
+          reinterpret_cast<__nv_bfloat16*>(stage)[32 * j + lane] = __float2bfloat16_rn(o * ms.alpha[32 * hh + j]);
+        }
         __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < kUnitHeads / 8; ++i) {
           const int idx = 32 * i + lane, hd = 32 * hh + (idx >> 2), d0 = 128 * c + 32 * q + 8 * (idx & 3);
           const uint4 v = *reinterpret_cast<const uint4*>(stage + 16 * idx);
           if (hd < heads_here) {
@@ -917,11 +1017,12 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
   }
 }
 
-// Two instances: kQImg, Q operand images from the prep kernel in the workspace
-// (the serving path), and without them, Q quantised here at each piece start;
-// the second's code stays out of the first (the kernel is bound by
-// instruction fetch).
-template <bool kQImg>
+// Instances by heads per CTA (NH = 64, or 16 for calls with at most 16 heads)
+// and by kQImg: Q operand images from the prep kernel in the workspace (the
+// serving path), or, without them, Q quantised here at each piece start; the
+// second's code stays out of the first (the kernel is bound by instruction
+// fetch).
+template <int NH, bool kQImg>
 __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __grid_constant__ DecodeArgs a,
                                                                   const __grid_constant__ CacheMaps maps) {
   // the merge kernel (launched next as a programmatic dependent) may be
@@ -929,28 +1030,28 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
   // complete before reading anything
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   uint8_t* sm = smem_base();
-  Misc& ms = *reinterpret_cast<Misc*>(sm + kOffMisc);
+  Misc& ms = *reinterpret_cast<Misc*>(sm + Form<NH>::kOffMisc);
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int head_base = head_block(a) * kNH;
-  const int heads_here = min(kNH, a.num_heads - head_base);
+  const int head_base = head_block<NH>(a) * NH;
+  const int heads_here = min(NH, a.num_heads - head_base);
 
   Sched sc;
   if (a.balanced) {
-    balanced_schedule<kThreads>(a, ms.sched, sc, cta_count(a), cta_index(a));
+    balanced_schedule<kThreads>(a, ms.sched, sc, cta_count<NH>(a), cta_index<NH>(a));
     if (sc.count == 0) {
       // An empty run (fewer tiles than CTAs) can sit inside the CTA span of
       // the sequence at its position; its slot of that sequence carries no weight.
       if (sc.pos0 < sc.total && tid < heads_here)
-        a.partial_lse[(static_cast<int64_t>(sc.b0) + cta_index(a)) * a.num_heads + head_base + tid] = -CUDART_INF_F;
+        a.partial_lse[(static_cast<int64_t>(sc.b0) + cta_index<NH>(a)) * a.num_heads + head_base + tid] = -CUDART_INF_F;
       return;  // (uniform: every thread read the same count)
     }
   } else {
     const int b = blockIdx.y, tiles = seq_tiles_of(a, b);
     const int per_split = (tiles + a.num_splits - 1) / a.num_splits;
     sc.b0 = b;
-    sc.off0 = cta_index(a) * per_split;
+    sc.off0 = cta_index<NH>(a) * per_split;
     sc.count = max(0, min(per_split, tiles - sc.off0));
     sc.pos0 = 0;
     sc.total = 0;
@@ -963,7 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
           *reinterpret_cast<uint32_t*>(a.o + b * a.o_stride_b + (head_base + h) * a.o_stride_h + d) = 0u;
         }
       } else if (tid < heads_here) {
-        a.partial_lse[(static_cast<int64_t>(b) * a.num_splits + cta_index(a)) * a.num_heads + head_base + tid] =
+        a.partial_lse[(static_cast<int64_t>(b) * a.num_splits + cta_index<NH>(a)) * a.num_heads + head_base + tid] =
             -CUDART_INF_F;
       }
       return;
@@ -1011,9 +1112,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
   if (warp >= kWarpQK) {
     setmaxnreg_dec<kIssuerRegs>();
     if (warp == kWarpQK) {
-      qk_issuer(sm, ms, tmem, sc, lane, a);
+      qk_issuer<NH>(sm, ms, tmem, sc, lane, a);
     } else if (warp < kWarpTMA) {
-      pv_issuer(sm, ms, tmem, sc, lane, warp - kWarpPV0, a);
+      pv_issuer<NH>(sm, ms, tmem, sc, lane, warp - kWarpPV0, a);
     } else if (lane == 0) {
       producer(sm, ms, sc, a, maps);
     }
@@ -1025,7 +1126,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
     loader(sm, ms, tmem, sc, warp, lane, a);
   } else {
     setmaxnreg_inc<kSoftmaxRegs>();
-    softmax<kQImg>(sm, ms, tmem, sc, head_base, heads_here, warp, lane, a.sm_scale * kLog2e, a);
+    softmax<NH, kQImg>(sm, ms, tmem, sc, head_base, heads_here, warp, lane, a.sm_scale * kLog2e, a);
   }
 
   fence_before_sync();
@@ -1038,43 +1139,40 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_fp4_kernel(const __gri
   }
 }
 
-// Q operand images of every (sequence, head block): one CTA of 1024 threads
+// Q operand images of every (sequence, head block): one CTA of 16 NH threads
 // each, thread (h, bl) quantising the 32-element block bl of head h (and the
 // 16-byte chunk bl < 8 of its q_pe).  It lets the decode kernel launched
 // after it start at once; that kernel waits for this grid before reading
 // the images.
-__global__ void __launch_bounds__(1024) q_prep_fp4_kernel(const __grid_constant__ DecodeArgs a) {
+template <int NH>
+__global__ void __launch_bounds__(16 * NH) q_prep_fp4_kernel(const __grid_constant__ DecodeArgs a) {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  const int b = blockIdx.y, head_base = blockIdx.x * kNH;
+  const int b = blockIdx.y, head_base = blockIdx.x * NH;
   const int h = threadIdx.x >> 4, bl = threadIdx.x & 15;
   const bool live = h < a.num_heads - head_base;
-  uint8_t* img = const_cast<uint8_t*>(a.q_img) + (static_cast<int64_t>(b) * gridDim.x + blockIdx.x) * kQImageBytes;
+  uint8_t* img =
+      const_cast<uint8_t*>(a.q_img) + (static_cast<int64_t>(b) * gridDim.x + blockIdx.x) * q_image_bytes(NH);
   const __nv_bfloat16* qrow = a.q + b * a.q_stride_b + (head_base + h) * a.q_stride_h;
   uint4 v[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) v[k] = ldg_stream_if(qrow + 32 * bl + 8 * k, live);
   const uint4 pe = ldg_stream_if(qrow + kLatent + 8 * (bl & 7), live && bl < 8);
-  q_block(v, h, bl, img, img + kQTermBytes + kQPeBytes);
-  if (bl < 8) *reinterpret_cast<uint4*>(img + kQTermBytes + (h >> 3) * 1024 + sw128_offset(h & 7, bl)) = pe;
+  q_block<NH>(v, h, bl, img, img + q_term_bytes(NH) + q_pe_bytes(NH));
+  if (bl < 8) *reinterpret_cast<uint4*>(img + q_term_bytes(NH) + (h >> 3) * 1024 + sw128_offset(h & 7, bl)) = pe;
 }
 
-}  // namespace
-
-cudaError_t launch_q_prep_fp4(const DecodeArgs& a, cudaStream_t stream) {
-  const dim3 grid((a.num_heads + kNH - 1) / kNH, a.batch);
-  q_prep_fp4_kernel<<<grid, 1024, 0, stream>>>(a);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(mla_decode_fp4_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+template <int NH>
+cudaError_t launch_decode_form(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream) {
+  constexpr int kSmem = smem_bytes<NH>();
+  cudaError_t e = cudaFuncSetAttribute(mla_decode_fp4_kernel<NH, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmem);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(mla_decode_fp4_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    e = cudaFuncSetAttribute(mla_decode_fp4_kernel<NH, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
-  const int head_blocks = (a.num_heads + kNH - 1) / kNH;
+  const int head_blocks = (a.num_heads + NH - 1) / NH;
   const dim3 grid = a.balanced ? dim3(a.num_splits * head_blocks, 1, 1) : dim3(a.num_splits * head_blocks, a.batch, 1);
   if (!a.q_img) {
-    mla_decode_fp4_kernel<false><<<grid, kThreads, kSmem, stream>>>(a, maps);
+    mla_decode_fp4_kernel<NH, false><<<grid, kThreads, kSmem, stream>>>(a, maps);
     return cudaGetLastError();
   }
   // after the Q prep kernel: start while it runs (everything before the Q
@@ -1089,7 +1187,23 @@ cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mla_decode_fp4_kernel<true>, a, maps);
+  return cudaLaunchKernelEx(&cfg, mla_decode_fp4_kernel<NH, true>, a, maps);
+}
+
+}  // namespace
+
+cudaError_t launch_q_prep_fp4(const DecodeArgs& a, cudaStream_t stream) {
+  if (decode_heads_per_cta(a.num_heads) == 16) {
+    q_prep_fp4_kernel<16><<<dim3((a.num_heads + 15) / 16, a.batch), 16 * 16, 0, stream>>>(a);
+  } else {
+    q_prep_fp4_kernel<64><<<dim3((a.num_heads + 63) / 64, a.batch), 16 * 64, 0, stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode_fp4(const DecodeArgs& a, const CacheMaps& maps, cudaStream_t stream) {
+  return decode_heads_per_cta(a.num_heads) == 16 ? launch_decode_form<16>(a, maps, stream)
+                                                 : launch_decode_form<64>(a, maps, stream);
 }
 
 }  // namespace kimi

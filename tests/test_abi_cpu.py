@@ -60,10 +60,20 @@ def test_device_status_argument_checks():
     assert lib.kimi_device_status(3, 0, None) == -4  # KIMI_ERR_MISALIGNED
 
 
-# Q operand images of the decode kernel per (sequence, 64-head block): three
-# e2m1 terms (2 x 192 x 128 B), q_pe (64 x 128 B) and the terms' e8m0 scales
-# (192 rows x 16 blocks)
-Q_IMAGE_BYTES = 2 * 192 * 128 + 64 * 128 + 192 * 16
+# Q operand images of the decode kernel per (sequence, head block of NH heads):
+# three e2m1 terms (2 x 3 NH x 128 B), q_pe (NH x 128 B) and the terms' e8m0
+# scales (3 NH rows x 16 blocks).  NH = 64, or 16 when the call has at most 16
+# heads.
+def q_image_bytes(nh):
+    return 2 * 3 * nh * 128 + nh * 128 + 3 * nh * 16
+
+
+def heads_per_block(h):
+    return 16 if h <= 16 else 64
+
+
+Q_IMAGE_BYTES = q_image_bytes(64)
+assert Q_IMAGE_BYTES == 60416 and q_image_bytes(16) == 15104
 
 
 def test_workspace_size_arithmetic():
@@ -77,20 +87,26 @@ def test_workspace_size_arithmetic():
     assert lib.kimi_mla_decode_workspace_size(b, h, s) == expect
     assert lib.kimi_mla_decode_workspace_size(b, h, 1) == 0  # single split writes o directly
     assert lib.kimi_mla_decode_workspace_size(b, 0, 4) == 0  # invalid
+    # 8 heads (a TP8 shard): one 16-head block per sequence
+    rows8 = b * s * 8
+    assert lib.kimi_mla_decode_workspace_size(b, 8, s) == (r256(rows8 * 512 * 2) + r256(rows8 * 4)
+                                                         + r256(b * 1 * q_image_bytes(16)))
     assert lib.kimi_mla_decode_num_splits(b, h, 7) == 7
     assert lib.kimi_mla_decode_num_splits(b, h, 999) == 64
 
 
 def test_balanced_workspace_size_arithmetic():
-    # num_kv_splits = 0: balanced schedule over G CTAs per 64-head block; the
+    # num_kv_splits = 0: balanced schedule over G CTAs per head block; the
     # workspace holds B + G partial slots plus one int2 CTA span per sequence
     lib = _lib.load()
-    for b, h in ((64, 64), (2, 16), (8, 128)):
+    for b, h in ((64, 64), (2, 16), (8, 128), (128, 8)):
         g = lib.kimi_mla_decode_num_splits(b, h, 0)
         assert g >= 1
         slots = b + g
         r256 = lambda n: ((n + 255) // 256) * 256
-        expect = r256(slots * h * 512 * 2) + r256(slots * h * 4) + r256(b * 8) + r256(b * -(-h // 64) * Q_IMAGE_BYTES)
+        nh = heads_per_block(h)
+        expect = (r256(slots * h * 512 * 2) + r256(slots * h * 4) + r256(b * 8)
+                  + r256(b * -(-h // nh) * q_image_bytes(nh)))
         assert lib.kimi_mla_decode_workspace_size(b, h, 0) == expect
     assert lib.kimi_mla_decode_num_splits(8, 128, 0) * 2 <= lib.kimi_mla_decode_num_splits(8, 64, 0) + 1
 

@@ -61,7 +61,11 @@ def test_balanced_agrees_with_split_mode_and_is_deterministic():
     auto = _decode(case)
     again = _decode(case)
     split = _decode(case, num_kv_splits=4)
-    assert np.array_equal(auto, again)
+    diff = np.argwhere(~((auto == again) | (np.isnan(auto) & np.isnan(again))))
+    assert diff.size == 0, (
+        f"{len(diff)} outputs differ between two identical calls; sequences {sorted(set(diff[:, 0].tolist()))}, "
+        f"heads {sorted(set(diff[:, 1].tolist()))[:16]}, latents {diff[:, 2].min()}..{diff[:, 2].max()}, "
+        f"NaN in the first call {int(np.isnan(auto).sum())}, in the second {int(np.isnan(again).sum())}")
     _check(case, auto)
     _check(case, split)
     assert np.abs(auto - split).max() <= 2 * MAX_ABS

@@ -279,19 +279,26 @@ def run_ours(args, rank, world, local_rank):
         barrier()
         ms_total = max_over_ranks(e0.elapsed_time(e1))
 
-        # ---- per-launch durations: events around each stage-1 launch and each merge ----
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * args.steps)]
-        for i in range(args.steps):
+        # ---- average launch durations: events around K back-to-back stage-1
+        # calls (the caches alternate, so every launch reads from HBM), then
+        # around K back-to-back merges of the last partials ----
+        def calls(i):
             w = wl[i % len(wl)]
-            call = (w["q"], w["kvb"], w["kvs"], w["o"], None, w["indptr"], w["perm"], w["last"])
-            ev[3 * i].record(stream)
-            kimi.mla_decode_partial(*call, sm_scale=SM_SCALE, workspace=w["ws"])
-            ev[3 * i + 1].record(stream)
-            kimi.mla_decode_merge(*call, sm_scale=SM_SCALE, workspace=w["ws"])
-            ev[3 * i + 2].record(stream)
+            return (w["q"], w["kvb"], w["kvs"], w["o"], None, w["indptr"], w["perm"], w["last"]), w["ws"]
+
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(stream)
+        for i in range(args.steps):
+            call, ws = calls(i)
+            kimi.mla_decode_partial(*call, sm_scale=SM_SCALE, workspace=ws)
+        ev[1].record(stream)
+        for i in range(args.steps):
+            call, ws = calls(args.steps - 1)
+            kimi.mla_decode_merge(*call, sm_scale=SM_SCALE, workspace=ws)
+        ev[2].record(stream)
         torch.cuda.synchronize()
-        stage1_ms = [ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(args.steps)]
-        merge_ms = [ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(args.steps)]
+        stage1_ms = [ev[0].elapsed_time(ev[1]) / args.steps]
+        merge_ms = [ev[1].elapsed_time(ev[2]) / args.steps]
 
         # ---- end to end through the public API with host buffers ----
         q_host = [torch.empty_like(w["q"], device="cpu").pin_memory() for w in wl]

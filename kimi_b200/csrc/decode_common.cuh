@@ -132,6 +132,27 @@ __device__ __forceinline__ uint4 half_group_to_e5m2(uint32_t w0, uint32_t w1, ui
   return o;
 }
 
+// (a0, a1) += (b0, b1) as one packed instruction: two round-to-nearest fp32
+// adds, the same results as two scalar adds.
+__device__ __forceinline__ void add_f32x2(float& a0, float& a1, float b0, float b1) {
+  uint64_t a = (static_cast<uint64_t>(__float_as_uint(a1)) << 32) | __float_as_uint(a0);
+  const uint64_t b = (static_cast<uint64_t>(__float_as_uint(b1)) << 32) | __float_as_uint(b0);
+  asm("add.rn.f32x2 %0, %0, %1;\n" : "+l"(a) : "l"(b));
+  a0 = __uint_as_float(static_cast<uint32_t>(a));
+  a1 = __uint_as_float(static_cast<uint32_t>(a >> 32));
+}
+
+// (a0, a1) = (a0, a1) * c + (d0, d1) as one packed instruction: two fused
+// round-to-nearest multiply-adds, the same results as two fmaf calls.
+__device__ __forceinline__ void fma_f32x2(float& a0, float& a1, float c, float d0, float d1) {
+  uint64_t a = (static_cast<uint64_t>(__float_as_uint(a1)) << 32) | __float_as_uint(a0);
+  const uint64_t cc = (static_cast<uint64_t>(__float_as_uint(c)) << 32) | __float_as_uint(c);
+  const uint64_t d = (static_cast<uint64_t>(__float_as_uint(d1)) << 32) | __float_as_uint(d0);
+  asm("fma.rn.f32x2 %0, %0, %1, %2;\n" : "+l"(a) : "l"(cc), "l"(d));
+  a0 = __uint_as_float(static_cast<uint32_t>(a));
+  a1 = __uint_as_float(static_cast<uint32_t>(a >> 32));
+}
+
 // p (two floats) -> e4m3 hi and e4m3 residual, through f16 (exact residual).
 __device__ __forceinline__ void split_e4m3x2(float p0, float p1, uint16_t& hi, uint16_t& lo) {
   uint32_t h;

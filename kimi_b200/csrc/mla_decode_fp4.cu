@@ -571,7 +571,6 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, in
     const uint8_t* nib = sm + kOffNib + s * kNibStage;
     const uint8_t* scb = sm + kOffSc + (j % kScSlots) * kScStage;
     const bool raw_ok = warp_wait(&ms.mb_rawfull[s], static_cast<uint32_t>((j >> 1) & 1), ms, a, 64, lane);
-    const int nvalid = cursor_valid(cur);
     // V'' quarter k: warp lw converts 4 tokens of the quarter's 8-token atom
     // lw / 2, rows {0, 2, 5, 7} (lw even) or {1, 3, 4, 6} (lw odd); lane l
     // the 32-element groups 8h + c, h = 0, 1, with c % 4 = l % 4 (bits 0-1),
@@ -590,11 +589,15 @@ __device__ void loader(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, in
           const uint4 nb =
               *reinterpret_cast<const uint4*>(nib + h * kNibBlock + (t >> 3) * 1024 + sw128_offset(t & 7, c));
           const int sbyte = scb[t * kScaleBytes + 8 * h + c];
+          // Rows past the tile's valid tokens (a tail page's unused slots, or
+          // stale bytes of a slot that was not loaded) are converted like the
+          // others: the exponent clamp keeps every byte finite (<= 6 * 2^13),
+          // and their P'' is exactly zero, so they add nothing to O.  Valid
+          // rows never reach the clamp (sigma keeps them at k <= 13).
           uint32_t lo, hi;
-          e5m2_tables(sbyte - 127 - sigma, lo, hi);
-          uint4 o0 = half_group_to_e5m2(nb.x, nb.y, lo, hi);
-          uint4 o1 = half_group_to_e5m2(nb.z, nb.w, lo, hi);
-          if (t >= nvalid) o0 = o1 = make_uint4(0u, 0u, 0u, 0u);
+          e5m2_tables(min(sbyte - 127 - sigma, 13), lo, hi);
+          const uint4 o0 = half_group_to_e5m2(nb.x, nb.y, lo, hi);
+          const uint4 o1 = half_group_to_e5m2(nb.z, nb.w, lo, hi);
           uint8_t* atom = sm + kOffV + (2 * h + (c >> 2)) * kVCol + (t >> 3) * 1024;
           *reinterpret_cast<uint4*>(atom + sw128_offset(t & 7, 2 * (c & 3))) = o0;
           *reinterpret_cast<uint4*>(atom + sw128_offset(t & 7, 2 * (c & 3) + 1)) = o1;
@@ -790,24 +793,36 @@ __device__ void softmax(uint8_t* sm, Misc& ms, uint32_t tmem, const Sched& sc, i
         tmem_ld_heads<HT>(tmem + lane_base + kColS + NH + HT * hf, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < HT; ++j) t[j] += __uint_as_float(sv[j]);
+        for (int j = 0; j < HT; j += 2) add_f32x2(t[j], t[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]));
         tmem_ld_heads<HT>(tmem + lane_base + kColS + 2 * NH + HT * hf, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < HT; ++j) t[j] += __uint_as_float(sv[j]);
+        for (int j = 0; j < HT; j += 2) add_f32x2(t[j], t[j + 1], __uint_as_float(sv[j]), __uint_as_float(sv[j + 1]));
       }
       fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ms.mb_sfree);
       ok = warp_wait(&ms.mb_sigready[tile & 3], static_cast<uint32_t>((tile >> 2) & 1), ms, a, 1, lane);
       sigma_cur = ms.sig[tile & 3];
-      const bool tvalid = st < cursor_valid(cur);
+      // x - R_h in log2 units; a full tile (every tile but a sequence's
+      // last) needs no per-token mask and takes packed multiply-adds
+      const int nvalid = cursor_valid(cur);
+      if (nvalid == 2 * kPageSize) {
 #pragma unroll
-      for (int j = 0; j < HT; j += 4) {
-        const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[HT * hf + j]);
-        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+        for (int j = 0; j < HT; j += 4) {
+          const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[HT * hf + j]);
+          fma_f32x2(t[j], t[j + 1], c_log2, -r4.x, -r4.y);
+          fma_f32x2(t[j + 2], t[j + 3], c_log2, -r4.z, -r4.w);
+        }
+      } else {
+        const bool tvalid = st < nvalid;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) t[j + u] = tvalid ? fmaf(t[j + u], c_log2, -rv[u]) : -CUDART_INF_F;
+        for (int j = 0; j < HT; j += 4) {
+          const float4 r4 = *reinterpret_cast<const float4*>(&ms.R[HT * hf + j]);
+          const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) t[j + u] = tvalid ? fmaf(t[j + u], c_log2, -rv[u]) : -CUDART_INF_F;
+        }
       }
     } else {
 #pragma unroll
